@@ -1,0 +1,508 @@
+"""Benchmark of the weight-only quantized GEMV hot path on B200.
+
+Default workload: the W8A16 lm_head GEMV with fused greedy argmax,
+int8 weights [151936, 2048] with per-row bf16 scales, one step = one call at each of
+M = 1, 4 and 16 tokens.  The weights (311 MB) exceed the 126 MB L2, so every call
+streams them from HBM.  Metric: HBM GB/s of algorithmic bytes (weights + scales +
+activations + logits + argmax), whole-job aggregate; µs per call is reported beside it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lm_head|draft_head|nvfp4|moe]
+    python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
+
+With N > 1 (torchrun, one rank per GPU, NCCL) the lm_head is vocab-sharded: each rank
+streams V/N rows, computes its shard's argmax keys, and one NCCL MAX all-reduce of the
+keys gives the global greedy token (strong scaling: total work fixed).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "µs/call and HBM GB/s (% of ~8 TB/s) for NVFP4 MoE & W8A16 GEMV at M=1–16"
+UNIT = "GB/s"
+FALLBACK_HBM = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["lm_head", "draft_head", "nvfp4", "moe"],
+                    default="lm_head")
+    ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM, "fallback (6.65 TB/s earlier pool measurement)"
+
+
+def traffic_for(workload: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = os.path.join(ROOT, "profiles", f"{workload}.traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------ clocks sampler
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.2)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_lm_head_sample(head_w, head_s, xs, rows: int, min_seconds: float):
+    """The reference's CPU path (dequantise then fp32 matmul, bf16 logits, argmax) on the
+    first `rows` rows, repeated for at least `min_seconds`.  Returns (GB/s, seconds, reps)."""
+    import numpy as np
+
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+    from oracle import w8a16 as ow8
+
+    w = head_w[:rows]
+    s = head_s[:rows]
+    K = w.shape[1]
+    nbytes = sum(syn.w8_head_bytes(rows, K, x.shape[0]) for x in xs)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for x in xs:
+            ow8.reference_cpu_path(x, w, "int8", s)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return nbytes * reps / el / 1e9, el, reps
+
+
+def run_reference(args):
+    """--impl reference: time the reference's CPU path (restated in numpy) on rank 0."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    V = syn.VOCAB if args.workload != "draft_head" else syn.DRAFT_VOCAB
+    rows = 1024
+    head = syn.w8_head(rows, syn.HIDDEN, seed=0)
+    w = head.w.numpy()
+    s = head.scale.float().numpy()
+    xs = [syn.activations(m, seed=1).float().numpy() for m in Ms]
+    from oracle import w8a16 as ow8
+
+    step_bytes = sum(syn.w8_head_bytes(rows, syn.HIDDEN, m) for m in Ms)
+    for _ in range(max(1, args.warmup)):
+        for x in xs:
+            ow8.reference_cpu_path(x, w, "int8", s)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for x in xs:
+            ow8.reference_cpu_path(x, w, "int8", s)
+    el = time.perf_counter() - t0
+    value = step_bytes * args.steps / el / 1e9
+    cores = os.cpu_count()
+    sample = (f"first {rows} of {V} rows of the int8 lm_head, M={Ms}, per step; numpy fp32 "
+              "dequantise + matmul + bf16 round + argmax")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8/bf16", "data": "synthetic",
+        "config": {"workload": f"w8a16_{args.workload}_{V}x{syn.HIDDEN}_argmax", "M": Ms},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import _lib
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _lib.lib()
+    fx.prealloc(dev)
+
+    if args.workload in ("lm_head", "draft_head"):
+        res = bench_lm_head(args, fx, syn, dev, rank, world)
+    elif args.workload == "nvfp4":
+        res = bench_nvfp4(args, fx, syn, dev)
+    else:
+        res = bench_moe(args, fx, syn, dev)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def _timed(fn, steps, warmup, dev, world, sampler=None):
+    """Device time (ms) of `steps` calls of fn, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        dist.barrier()
+    ms = s.elapsed_time(e)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, clocks
+
+
+def _gpu_id(dev):
+    import torch
+
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index)
+
+
+def bench_lm_head(args, fx, syn, dev, rank, world):
+    import torch
+    import torch.distributed as dist
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    V = syn.VOCAB if args.workload == "lm_head" else syn.DRAFT_VOCAB
+    K = syn.HIDDEN
+    if V % world:
+        raise SystemExit(f"vocab {V} not divisible by {world} ranks")
+    shard = V // world
+    # every rank generates the full seeded head and keeps its own row slice
+    head = syn.w8_head(V, K, seed=0)
+    r0 = rank * shard
+    w = head.w[r0:r0 + shard].contiguous().to(dev)
+    s = head.scale[r0:r0 + shard].contiguous().to(dev)
+    xs = [syn.activations(m, seed=1).to(dev) for m in Ms]
+    ys = [torch.empty(m, shard, dtype=torch.bfloat16, device=dev) for m in Ms]
+    ams = [torch.empty(m, dtype=torch.int64, device=dev) for m in Ms]
+    keys = [torch.empty(m, dtype=torch.int64, device=dev) for m in Ms]
+    lib = _lib_handle()
+    import ctypes
+
+    from flash_next_rtxpro6000_b200.w8a16_gemv import _workspace
+
+    ws = _workspace(dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    pdl = 1
+
+    def call(i, x):
+        # the operator API's C call, with the raw key output for the sharded reduction
+        rc = lib.fnx_w8a16_gemv(
+            x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), _lib.W_INT8, s.data_ptr(),
+            _lib.SCALE_BF16_ROW, ys[i].data_ptr(), ys[i].stride(0), None, 0, 0, 0,
+            ams[i].data_ptr() if world == 1 else None,
+            keys[i].data_ptr() if world > 1 else None, r0, x.shape[0], shard, K, None,
+            ctypes.byref(ws.c), pdl, stream)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    def step():
+        for i, x in enumerate(xs):
+            call(i, x)
+            if world > 1:
+                dist.all_reduce(keys[i], op=dist.ReduceOp.MAX)
+                lib.fnx_argmax_decode(keys[i].data_ptr(), ams[i].data_ptr(), x.shape[0], stream)
+
+    # per-M kernel durations (for the roofline and µs/call): back-to-back launches
+    per_m = {}
+    for i, x in enumerate(xs):
+        reps = max(50, args.steps // 4)
+        ms_i, _ = _timed(lambda: call(i, x), reps, max(3, args.warmup // 4), dev, world)
+        per_m[Ms[i]] = ms_i / reps * 1e3  # µs per launch
+    sampler = ClockSampler(_gpu_id(dev)) if rank == 0 else None
+    ms, clocks = _timed(step, args.steps, max(3, args.warmup), dev, world, sampler)
+    total_bytes_step = sum(syn.w8_head_bytes(V, K, m) for m in Ms)
+    value = total_bytes_step * args.steps / (ms / 1e3) / 1e9
+    peak, peak_src = measured_peak()
+    # roofline of the GEMV kernel: per-launch algorithmic bytes of this rank's shard
+    kbytes = sum(syn.w8_head_bytes(shard, K, m) for m in Ms)
+    kus = sum(per_m.values())
+    achieved = kbytes / (kus * 1e-6) / 1e9
+    traffic = traffic_for(f"dense_gemv_int8_{args.workload}")
+    tr = None
+    if traffic and world == 1:
+        tr = sum(traffic.get(str(m), 0) for m in Ms) / max(1, len(Ms))
+    res = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8/bf16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"w8a16_{args.workload}_{V}x{K}_argmax", "M": Ms,
+                   "weights": "int8 per-row bf16 scale", "l2": "weights 311 MB > 126 MB L2, no flush needed",
+                   "parallelism": f"vocab-sharded x{world} + NCCL MAX all-reduce of argmax keys"
+                   if world > 1 else "single GPU"},
+        "us_per_call": {str(m): round(v, 3) for m, v in per_m.items()},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": tr, "peak_source": peak_src,
+                     "kernel": "dense_gemv_kernel<int8>", "bytes_per_launch_avg": kbytes // len(Ms)},
+        "clocks": clocks,
+        "gpu_launches": args.steps * len(Ms) * (2 if world > 1 else 1),
+    }
+    if not args.no_e2e:
+        res["e2e"] = e2e_lm_head(args, fx, syn, dev, w, s, Ms, world, rank, r0, shard, V, K)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import numpy as np
+
+        xs_np = [x.float().cpu().numpy() for x in xs]
+        gbs, el, reps = cpu_lm_head_sample(head.w.numpy(), head.scale.float().numpy(), xs_np,
+                                           rows=16384, min_seconds=10.0)
+        res["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": os.cpu_count(),
+                               "kind": "port",
+                               "sample": f"16384 of {V} rows, M={Ms}, {reps} reps in {el:.1f} s "
+                                         "(numpy fp32 dequantise+matmul, bf16 round, argmax)"}
+    return res
+
+
+def _lib_handle():
+    from flash_next_rtxpro6000_b200 import _lib
+
+    return _lib.lib()
+
+
+def e2e_lm_head(args, fx, syn, dev, w, s, Ms, world, rank, r0, shard, V, K):
+    """Public API end to end: pinned host x -> device, w8a16_gemv(argmax_out=...),
+    argmax -> pinned host, one host sync per step."""
+    import torch
+    import torch.distributed as dist
+
+    hx = [syn.activations(m, seed=1).pin_memory() for m in Ms]
+    dx = [torch.empty(m, K, dtype=torch.bfloat16, device=dev) for m in Ms]
+    dam = [torch.empty(m, dtype=torch.int64, device=dev) for m in Ms]
+    ham = [torch.empty(m, dtype=torch.int64).pin_memory() for m in Ms]
+    ys = [torch.empty(m, shard, dtype=torch.bfloat16, device=dev) for m in Ms]
+    from flash_next_rtxpro6000_b200 import sharded
+
+    def step():
+        for i, m in enumerate(Ms):
+            dx[i].copy_(hx[i], non_blocking=True)
+            if world == 1:
+                fx.w8a16_gemv(dx[i], w, s, out=ys[i], argmax_out=dam[i], pdl=True)
+            else:
+                sharded.sharded_lm_head_argmax(dx[i], w, s, r0, out=ys[i], argmax_out=dam[i])
+            ham[i].copy_(dam[i], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    steps = max(20, args.steps // 4)
+    ms, _ = _timed(step, steps, max(3, args.warmup // 4), dev, world)
+    total = sum(syn.w8_head_bytes(V, K, m) for m in Ms)
+    return {"value": round(total * steps / (ms / 1e3) / 1e9, 2), "unit": UNIT,
+            "h2d_bytes_per_step": sum(m * K * 2 for m in Ms),
+            "d2h_bytes_per_step": sum(m * 8 for m in Ms), "steps": steps}
+
+
+def bench_nvfp4(args, fx, syn, dev):
+    """Config 0 (NVFP4 4096 x 2048): 64 weight copies rotated (> 4x L2)."""
+    import torch
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    copies = 64
+    ws = [syn.nvfp4_weight(syn.NVFP4_N, syn.HIDDEN, seed=i) for i in range(copies)]
+    ws = [(w.wq.to(dev), w.bs.to(dev), w.gscale.to(dev)) for w in ws]
+    xs = [syn.activations(m, seed=1).to(dev) for m in Ms]
+    ys = [torch.empty(m, syn.NVFP4_N, dtype=torch.bfloat16, device=dev) for m in Ms]
+    it = [0]
+
+    def step():
+        for i, x in enumerate(xs):
+            wq, bs, g = ws[it[0] % copies]
+            it[0] += 1
+            fx.w4a16_nvfp4_gemv(x, wq, bs, g, out=ys[i], pdl=True)
+
+    sampler = ClockSampler(_gpu_id(dev))
+    ms, clocks = _timed(step, args.steps, max(3, args.warmup), dev, 1, sampler)
+    per_step = sum(syn.nvfp4_bytes(syn.NVFP4_N, syn.HIDDEN, m) for m in Ms)
+    value = per_step * args.steps / (ms / 1e3) / 1e9
+    peak, src = measured_peak()
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": "nvfp4_gemv_4096x2048", "M": Ms,
+                       "l2": f"{copies} weight copies rotated (> 4x L2)"},
+            "us_per_call": round(ms / args.steps / len(Ms) * 1e3, 3),
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": args.steps * len(Ms)}
+
+
+def bench_moe(args, fx, syn, dev):
+    """Config 2 (NVFP4 MoE, 512 experts, top-10 + shared expert).  Routings rotate over
+    disjoint expert sets so the weights come from HBM (> 4x L2 across the rotation)."""
+    import numpy as np
+    import torch
+
+    from flash_next_rtxpro6000_b200.w4a16_nvfp4_gemv import swizzle_blockscale
+
+    Ms = [int(m) for m in (args.ms or "1,2,4,8,16").split(",")]
+    L = syn.moe_layer(syn.EXPERTS, syn.HIDDEN, syn.INTER, seed=0)
+    d = dict(w13=L.w13.to(dev), s13=swizzle_blockscale(L.s13.to(dev)), g13=L.g13.to(dev),
+             w2=L.w2.to(dev), s2=swizzle_blockscale(L.s2.to(dev)), g2=L.g2.to(dev))
+    shared = fx.SharedExpert(L.sh_w13.to(dev), swizzle_blockscale(L.sh_s13.to(dev)),
+                             L.sh_g13.to(dev), L.sh_w2.to(dev), swizzle_blockscale(L.sh_s2.to(dev)),
+                             L.sh_g2.to(dev))
+    ws = fx.make_workspace(num_routes=10, hidden_size=syn.HIDDEN, intermediate_size=syn.INTER,
+                           device=dev)
+    results = {}
+    peak, src = measured_peak()
+    total_bytes, total_ms = 0, 0.0
+    sampler = ClockSampler(_gpu_id(dev))
+    for M in Ms:
+        n_rot = 48
+        rots = []
+        nbytes = 0
+        for r in range(n_rot):
+            ids, wts = syn.routing(M, E=syn.EXPERTS, seed=1000 * M + r)
+            # shift expert ids by a rotation-dependent offset: successive calls touch
+            # different experts, as consecutive decode layers do
+            ids = ((ids.long() + 97 * r) % syn.EXPERTS).to(torch.int32)
+            D = int(torch.unique(ids).numel())
+            nbytes += syn.moe_bytes(D, M=M)
+            rots.append((ids.to(dev), wts.to(dev)))
+        x = syn.activations(M, seed=3).to(dev)
+        out = torch.empty(M, syn.HIDDEN, dtype=torch.bfloat16, device=dev)
+        it = [0]
+
+        def step():
+            ids, wts = rots[it[0] % n_rot]
+            it[0] += 1
+            fx.draft_moe_gemv(hidden_states=x, topk_ids=ids, topk_weights=wts,
+                              w13_weight=d["w13"], w13_blockscale_swizzled=d["s13"],
+                              w13_weight_scale_2=d["g13"], w2_weight=d["w2"],
+                              w2_blockscale_swizzled=d["s2"], w2_weight_scale_2=d["g2"],
+                              workspace=ws, shared_expert=shared, out=out)
+
+        steps = (args.steps // n_rot + 1) * n_rot
+        ms, clocks = _timed(step, steps, max(n_rot, args.warmup), dev, 1, sampler if M == Ms[-1] else None)
+        bytes_per_call = nbytes / n_rot
+        us = ms / steps * 1e3
+        results[str(M)] = {"us_per_call": round(us, 3),
+                           "GBps": round(bytes_per_call / (us * 1e-6) / 1e9, 1),
+                           "bytes_per_call": int(bytes_per_call)}
+        total_bytes += bytes_per_call * steps
+        total_ms += ms
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / max(1, args.steps), 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/bf16 (fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
+                       "l2": "48 routings over rotated expert sets (> 4x L2)"},
+            "per_m": results,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": 2 * sum(1 for _ in Ms) * args.steps}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,41 @@
+"""B200 (sm_100a) weight-only quantized GEMV for decode and verify widths (M <= 16).
+
+Operators (host mirrors of the reference's kernels/sglang operator modules, computed by
+the hand-written CUDA library ``_fnx.so``):
+
+* ``w8a16_gemv``, ``bf16_gemv``, ``w8a16_gemv_silu_mul`` -- W8A16 (int8 / fp8) GEMV,
+  the lm_head and draft-head path, with fused greedy argmax;
+* ``w4a16_nvfp4_gemv`` -- NVFP4 GEMV; ``quantize_nvfp4`` / ``dequantize_nvfp4`` codec;
+* ``draft_moe_gemv`` / ``moe_gemv`` -- routed NVFP4 MoE expert GEMVs (gate_up + SiLU,
+  down + router-weighted route sum), M <= 16;
+* ``sharded`` -- vocab-sharded lm_head and expert-sharded MoE over torch.distributed.
+"""
+
+from .w8a16_gemv import (  # noqa: F401
+    GemvConfig,
+    bf16_gemv,
+    prealloc,
+    scratch_slot,
+    w8a16_gemv,
+    w8a16_gemv_silu_mul,
+    w8a16_gemv_silu_mul_supported,
+)
+from .w4a16_nvfp4_gemv import (  # noqa: F401
+    dequantize_nvfp4,
+    quantize_nvfp4,
+    swizzle_blockscale,
+    w4a16_nvfp4_gemv,
+)
+from .draft_moe_gemv import (  # noqa: F401
+    DEFAULT_CONFIG,
+    DraftMoeGemvConfig,
+    DraftMoeGemvRunner,
+    SharedExpert,
+    draft_moe_gemv,
+    enable_draft_moe_gemv,
+    make_workspace,
+    moe_gemv,
+    unsupported_reason,
+)
+
+__version__ = "0.1.0"

@@ -1,0 +1,157 @@
+"""ctypes binding of the C ABI in include/fnx_gemv.h.
+
+The library is the product: there is no Python or torch fallback.  If ``_fnx.so`` is
+missing, importing an operator raises, naming the build command.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_char_p, c_int, c_int64, c_void_p
+
+from .build import LIB_PATH
+
+FNX_OK, FNX_EINVAL, FNX_ECUDA, FNX_EUNSUPPORTED = 0, 1, 2, 3
+W_INT8, W_FP8_E4M3, W_BF16, W_NVFP4 = 0, 1, 2, 3
+SCALE_NONE, SCALE_F32_SCALAR, SCALE_F32_ROW, SCALE_BF16_SCALAR, SCALE_BF16_ROW = 0, 1, 2, 3, 4
+MAX_M = 16
+
+EXPORTED = (
+    "fnx_plan_gemv",
+    "fnx_gemv_workspace_need",
+    "fnx_w8a16_gemv",
+    "fnx_w8a16_gemv_silu_mul",
+    "fnx_w4a16_nvfp4_gemv",
+    "fnx_moe_workspace_bytes",
+    "fnx_moe_gemv",
+    "fnx_argmax_decode",
+    "fnx_last_error",
+    "fnx_version",
+)
+
+
+class FnxWorkspace(ctypes.Structure):
+    _fields_ = [
+        ("partials", c_void_p),
+        ("partial_floats", c_int64),
+        ("counters", c_void_p),
+        ("n_counters", c_int64),
+        ("argmax_keys", c_void_p),
+        ("argmax_count", c_void_p),
+    ]
+
+
+class FnxGemvCfg(ctypes.Structure):
+    _fields_ = [
+        ("warps", c_int),
+        ("chunks_per_warp", c_int),
+        ("groups", c_int),
+        ("ksplit", c_int),
+        ("grid", c_int),
+    ]
+
+
+class FnxMoeWeights(ctypes.Structure):
+    _fields_ = [
+        ("w13", c_void_p),
+        ("w13_scale", c_void_p),
+        ("w13_gscale", c_void_p),
+        ("w13_gscale_stride", c_int64),
+        ("w2", c_void_p),
+        ("w2_scale", c_void_p),
+        ("w2_gscale", c_void_p),
+        ("w2_gscale_stride", c_int64),
+        ("num_experts", c_int),
+        ("expert_offset", c_int),
+        ("hidden", c_int),
+        ("inter", c_int),
+        ("scales_swizzled", c_int),
+    ]
+
+
+class FnxMoeWorkspace(ctypes.Structure):
+    _fields_ = [
+        ("act", c_void_p),
+        ("partials", c_void_p),
+        ("counters", c_void_p),
+        ("max_m", c_int),
+        ("max_routes", c_int),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+_P = c_void_p
+_I64P = POINTER(c_int64)
+
+
+def _declare(lib):
+    lib.fnx_plan_gemv.argtypes = [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(FnxGemvCfg)]
+    lib.fnx_gemv_workspace_need.argtypes = [c_int, c_int, c_int, c_int, c_int,
+                                            POINTER(FnxGemvCfg), _I64P, _I64P]
+    lib.fnx_w8a16_gemv.argtypes = [
+        _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, _P, c_int64, c_int64, c_int,
+        _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int,
+        _P]
+    lib.fnx_w8a16_gemv_silu_mul.argtypes = [
+        _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, c_int, c_int, c_int,
+        POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_w4a16_nvfp4_gemv.argtypes = [
+        _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
+        c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),
+        POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_moe_workspace_bytes.argtypes = [c_int, c_int, c_int, c_int, _I64P, _I64P, _I64P]
+    lib.fnx_moe_gemv.argtypes = [
+        _P, c_int64, _P, _P, c_int, c_int, POINTER(FnxMoeWeights), POINTER(FnxMoeWeights), _P,
+        c_int64, c_int, POINTER(FnxMoeWorkspace), c_int, _P]
+    lib.fnx_argmax_decode.argtypes = [_P, _P, c_int, _P]
+    lib.fnx_last_error.restype = c_char_p
+    lib.fnx_version.restype = c_char_p
+    for name in EXPORTED:
+        if name not in ("fnx_last_error", "fnx_version"):
+            getattr(lib, name).restype = c_int
+
+
+def lib():
+    """The loaded library (built on first use when nvcc is available)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                try:
+                    from .build import build
+
+                    build()
+                except Exception as e:  # pragma: no cover - depends on the toolchain
+                    raise ImportError(
+                        f"{LIB_PATH.name} is missing and could not be built ({e}); run "
+                        "`python -m flash_next_rtxpro6000_b200.build` on a machine with nvcc"
+                    ) from e
+            handle = ctypes.CDLL(str(LIB_PATH))
+            _declare(handle)
+            _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().fnx_last_error().decode("utf-8", "replace")
+
+
+def check(rc: int, what: str) -> None:
+    """Raise the Python exception the reference raises for the same condition."""
+    if rc == FNX_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc == FNX_EINVAL:
+        raise ValueError(msg)
+    if rc == FNX_EUNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)
+
+
+def ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())

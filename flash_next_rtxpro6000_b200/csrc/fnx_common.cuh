@@ -1,0 +1,420 @@
+// Shared device building blocks of the weight-only quantized GEMV kernels (sm_100a).
+//
+// Every kernel in this library computes y[m, n] = sum_k W[n, k] * x[m, k] for M <= 16
+// tokens by streaming the weight rows once from HBM.  The arithmetic is done on the
+// tensor cores with `mma.sync.m16n8k16` in "swap-AB" form: the weights are the 16-row A
+// operand and the (at most 16) tokens are the 8-wide B operand, so one instruction covers
+// 256 weights and the CUDA cores only have to dequantise.
+//
+// Numerics (these follow the reference's own exactness argument,
+// kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:25-29):
+//  * an int8 weight, an fp8 e4m3 weight and an e2m1 * e4m3 NVFP4 product are all exact
+//    in fp16, so the A operand is the exact dequantised weight;
+//  * the activations are bf16.  They are multiplied by a per-token power of two chosen
+//    from the row's max |x| (so the largest element lands in [2^14, 2^15)) and then
+//    converted to fp16, which is exact for every element within 2^-31 of the row max
+//    (smaller ones are rounded to the fp16 subnormal grid, an absolute error below
+//    2^-40 of the row max).  The epilogue multiplies by the inverse power of two, which
+//    is exact, so the result equals an fp32-accumulated dot of the bf16 inputs;
+//  * accumulation is fp32 in the tensor core; the per-row scale is applied once per
+//    output after the k reduction (w8a16_gemv.py:266-270) and the result is rounded to
+//    bf16 before any fp32 widening (w8a16_gemv.py:92-95).
+//
+// k permutation.  The reduction over k is order-free, so each lane reads 16 contiguous
+// bytes of a weight row (one 128-bit load) and the fragment slots of MMA j map to
+// k0 = c*T + 4j + {0,1,2,3} (c = lane % 4, T = k per lane per chunk).  The B fragment of
+// the same MMA then needs x[token][k0 .. k0+3], which the staging below stores in exactly
+// that order, so the x fragments are conflict-free 128-bit shared-memory loads.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace fnx {
+
+// Weight element formats (values are part of the C ABI, include/fnx_gemv.h).
+enum WType : int { W_INT8 = 0, W_FP8 = 1, W_BF16 = 2, W_NVFP4 = 3 };
+
+// Per-row (or scalar) output scale formats (C ABI values).
+enum ScaleKind : int {
+  SCALE_NONE = 0,      // 1.0
+  SCALE_F32_SCALAR = 1,
+  SCALE_F32_ROW = 2,
+  SCALE_BF16_SCALAR = 3,
+  SCALE_BF16_ROW = 4,
+};
+
+// One "chunk" is 64 bytes of one weight row per group of four lanes (16 B per lane).
+template <int WT> struct WTraits;
+template <> struct WTraits<W_INT8> { static constexpr int T = 16; };   // k per lane per chunk
+template <> struct WTraits<W_FP8> { static constexpr int T = 16; };
+template <> struct WTraits<W_BF16> { static constexpr int T = 8; };
+template <> struct WTraits<W_NVFP4> { static constexpr int T = 32; };
+
+template <int WT> struct Geo {
+  static constexpr int T = WTraits<WT>::T;
+  static constexpr int CH = 4 * T;        // k per chunk (all four lanes of a row)
+  static constexpr int MMAS = T / 4;      // m16n8k16 instructions per chunk
+  static constexpr int Q = T / 8;         // 16-byte x units per lane per chunk
+};
+
+// ------------------------------------------------------------------------------------
+// Global loads
+// ------------------------------------------------------------------------------------
+
+// Streaming weight load: read-only path, no L1 allocation, L2 evict-first so the
+// weights (read exactly once per call) do not push activations and scratch out of L2.
+__device__ __forceinline__ uint4 ldg_stream(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile(
+      "ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_u16_stream(const void* p, uint64_t pol) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u16 %0, [%1], %2;"
+               : "=h"(v)
+               : "l"(p), "l"(pol));
+  return (uint32_t)v;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Loads that must observe other CTAs' writes of this same launch (split-K partials,
+// MoE partials): bypass L1.
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_cg_f32(float* p, float v) {
+  asm volatile("st.global.cg.f32 [%0], %1;" ::"l"(p), "f"(v));
+}
+
+// ------------------------------------------------------------------------------------
+// Programmatic dependent launch (the B200 form of the reference's PDL helpers,
+// kernels/sglang/kernels/triton_pdl.py:60-83).  Both are no-ops when the launch did
+// not set the programmatic-serialization attribute.
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Named barrier over `nthreads` threads (a group of warps inside the CTA).
+__device__ __forceinline__ void group_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------------------------------------
+// Dequantisation of one 32-bit word of a weight row into two fp16x2 A-fragment halves:
+// `lo` holds k0, k0+1 and `hi` holds k0+2, k0+3 (low half = lower k).
+// ------------------------------------------------------------------------------------
+
+// int8: XOR 0x80 maps the signed byte b to u = b + 128; 0x6400 | u is the fp16 value
+// 1024 + u, and subtracting 1152 leaves b exactly.
+__device__ __forceinline__ void deq_int8_word(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
+  uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+  const uint32_t bias = 0x64806480u;  // fp16 1152.0 in both halves
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(bias));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(bias));
+}
+
+// fp8 e4m3: native packed conversion (lower byte -> lower half).
+__device__ __forceinline__ void deq_fp8_word(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"((unsigned short)(w & 0xFFFFu)));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"((unsigned short)(w >> 16)));
+}
+
+// NVFP4: four bytes = eight e2m1 codes, low nibble = even k
+// (w4a16_nvfp4_gemv.py:7-8).  Each byte becomes one fp16x2 (low nibble -> low half).
+__device__ __forceinline__ void deq_e2m1_word(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 q0, q1, q2, q3;\n\t"
+      "mov.b32 {q0, q1, q2, q3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, q0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, q1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, q2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, q3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
+// Two e4m3 block scales (lower byte = lower k block) -> fp16x2.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((unsigned short)two_bytes));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Broadcast the low / high fp16 of a pair to both halves.
+__device__ __forceinline__ uint32_t bcast_lo(uint32_t v) { return __byte_perm(v, 0, 0x1010); }
+__device__ __forceinline__ uint32_t bcast_hi(uint32_t v) { return __byte_perm(v, 0, 0x3232); }
+
+// ------------------------------------------------------------------------------------
+// Tensor-core MMA (fp32 accumulate).
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------------------------------
+// One chunk of one lane: 16 B of row g (va) and row g+8 (vb), their NVFP4 block scales
+// (sa, sb: two e4m3 bytes each) and the B fragments; accumulates into acc[nt][4].
+// xs points at this lane's 16-byte x units for token (nt*8 + g); the unit q of the
+// chunk holds k0 .. k0+7 of MMAs 2q and 2q+1.
+// ------------------------------------------------------------------------------------
+template <int WT, int NT>
+__device__ __forceinline__ void chunk_mma(float (&acc)[NT][4], const uint4& va, const uint4& vb,
+                                          uint32_t sa, uint32_t sb,
+                                          const uint4 (&xf)[NT][Geo<WT>::Q], int nt_act = NT) {
+  const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+  const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+  if constexpr (WT == W_INT8 || WT == W_FP8) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t a0, a2, a1, a3;
+      if constexpr (WT == W_INT8) {
+        deq_int8_word(wa[j], a0, a2);
+        deq_int8_word(wb[j], a1, a3);
+      } else {
+        deq_fp8_word(wa[j], a0, a2);
+        deq_fp8_word(wb[j], a1, a3);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (nt >= nt_act) break;
+        const uint4& u = xf[nt][j >> 1];
+        const uint32_t b0 = (j & 1) ? u.z : u.x;
+        const uint32_t b1 = (j & 1) ? u.w : u.y;
+        mma_f16(acc[nt], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  } else if constexpr (WT == W_BF16) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t a0 = wa[2 * j], a2 = wa[2 * j + 1];
+      const uint32_t a1 = wb[2 * j], a3 = wb[2 * j + 1];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (nt >= nt_act) break;
+        const uint4& u = xf[nt][0];
+        const uint32_t b0 = j ? u.z : u.x;
+        const uint32_t b1 = j ? u.w : u.y;
+        mma_bf16(acc[nt], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  } else {  // W_NVFP4
+    const uint32_t sfa = e4m3x2_to_f16x2(sa);
+    const uint32_t sfb = e4m3x2_to_f16x2(sb);
+    const uint32_t sa0 = bcast_lo(sfa), sa1 = bcast_hi(sfa);
+    const uint32_t sb0 = bcast_lo(sfb), sb1 = bcast_hi(sfb);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // word q serves MMAs 2q (byte 0,1) and 2q+1 (byte 2,3)
+      uint32_t ha[4], hb[4];
+      deq_e2m1_word(wa[q], ha);
+      deq_e2m1_word(wb[q], hb);
+      const uint32_t s_a = (q < 2) ? sa0 : sa1;
+      const uint32_t s_b = (q < 2) ? sb0 : sb1;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * q + h;
+        const uint32_t a0 = hmul2(ha[2 * h], s_a);
+        const uint32_t a2 = hmul2(ha[2 * h + 1], s_a);
+        const uint32_t a1 = hmul2(hb[2 * h], s_b);
+        const uint32_t a3 = hmul2(hb[2 * h + 1], s_b);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (nt >= nt_act) break;
+          const uint4& u = xf[nt][j >> 1];
+          const uint32_t b0 = (j & 1) ? u.z : u.x;
+          const uint32_t b1 = (j & 1) ? u.w : u.y;
+          mma_f16(acc[nt], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Activation staging.  A staged row (token or MoE route pair) is K fp16 (or bf16 for a
+// bf16 weight) stored in 16-byte units; unit (chunk, q, c) holds
+// k = chunk*CH + c*T + q*8 .. +7 at byte offset ((chunk*Q + q)*4 + c)*16.  The row
+// stride is 2K + 64 bytes, so the eight lanes of one 128-bit load phase (two rows, four
+// lanes each) hit eight distinct 16-byte bank groups.
+// ------------------------------------------------------------------------------------
+__host__ __device__ constexpr int stage_row_bytes(int K) { return 2 * K + 64; }
+
+template <int WT>
+__device__ __forceinline__ int stage_unit_offset(int k) {  // k multiple of 8
+  constexpr int CH = Geo<WT>::CH, T = Geo<WT>::T, Q = Geo<WT>::Q;
+  const int chunk = k / CH;
+  const int rem = k - chunk * CH;
+  const int c = rem / T;
+  const int q = (rem - c * T) >> 3;
+  return ((chunk * Q + q) * 4 + c) * 16;
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) {
+  return __uint_as_float(b16 << 16);
+}
+
+// Exponent e such that max_abs * 2^e lies in [2^14, 2^15); 0 for an all-zero row.
+__device__ __forceinline__ int stage_exponent(float max_abs) {
+  if (!(max_abs > 0.f)) return 0;
+  const uint32_t bits = __float_as_uint(max_abs);
+  int ex = (int)((bits >> 23) & 0xFF) - 127;  // floor(log2) for normals; -127 for denormals
+  int e = 14 - ex;
+  if (e > 100) e = 100;
+  if (e < -40) e = -40;
+  return e;
+}
+
+__device__ __forceinline__ float pow2f(int e) {  // exact for e in [-126, 127]
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
+// Convert 8 bf16 (a 16-byte vector) to 8 fp16 scaled by 2^e (e in [-40, 100], so the
+// factor is a normal float and the multiply is exact before the fp16 rounding).
+__device__ __forceinline__ uint4 bf16x8_to_f16x8_scaled(const uint4 v, int e) {
+  const float f = pow2f(e);
+  const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+  uint32_t out[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = bf16_bits_to_f32(in[i] & 0xFFFFu) * f;
+    const float hi = bf16_bits_to_f32(in[i] >> 16) * f;
+    const __half2 h = __floats2half2_rn(lo, hi);
+    out[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+__device__ __forceinline__ float bf16x8_absmax(const uint4 v) {
+  const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m = fmaxf(m, fabsf(bf16_bits_to_f32(in[i] & 0xFFFFu)));
+    m = fmaxf(m, fabsf(bf16_bits_to_f32(in[i] >> 16)));
+  }
+  return m;
+}
+
+// Order-preserving 16-bit key of a bf16 value for the greedy argmax: larger value ->
+// larger key; -0 is folded onto +0 so that equal logits tie (torch.argmax semantics).
+__device__ __forceinline__ uint32_t bf16_order_key(uint32_t b) {
+  b &= 0xFFFFu;
+  if (b == 0x8000u) b = 0;
+  return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+}
+
+// argmax key: value key in the high 32 bits, (0xFFFFFFFF - index) in the low 32 bits, so
+// the maximum key is the largest value and, among equal values, the lowest index.
+__device__ __forceinline__ unsigned long long argmax_key(uint32_t bf16_bits, uint32_t index) {
+  return ((unsigned long long)bf16_order_key(bf16_bits) << 32) |
+         (unsigned long long)(0xFFFFFFFFu - index);
+}
+
+__device__ __forceinline__ float load_row_scale(const void* scale, int kind, int64_t n) {
+  switch (kind) {
+    case SCALE_F32_SCALAR: return __ldg(reinterpret_cast<const float*>(scale));
+    case SCALE_F32_ROW: return __ldg(reinterpret_cast<const float*>(scale) + n);
+    case SCALE_BF16_SCALAR:
+      return bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(scale)));
+    case SCALE_BF16_ROW:
+      return bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(scale) + n));
+    default: return 1.f;
+  }
+}
+
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
+
+__device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Stage `nrows` activation rows of K bf16 into shared memory in the fragment order above.
+// Row r is read from src(r) (a bf16 pointer, or nullptr for a row that is never used).
+// Each warp takes one row: pass 1 finds max |x|, pass 2 converts with the row's power of
+// two (fp16) or copies it unchanged (bf16 weights, `keep_bf16`).  unscale[r] receives
+// the inverse power of two that the epilogue applies.  Reads use ld.global.cg: the rows
+// may have been written by the previous kernel of a programmatic-dependent pair.
+template <int WT, typename SrcFn>
+__device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int K,
+                                           SrcFn src) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int srow = stage_row_bytes(K);
+  const int units = K >> 3;
+  for (int r = warp; r < nrows; r += nwarps) {
+    const __nv_bfloat16* p = src(r);
+    if (p == nullptr) {
+      if (lane == 0) unscale[r] = 0.f;
+      continue;
+    }
+    uint8_t* dst = xs + (size_t)r * srow;
+    if constexpr (WT == W_BF16) {
+      for (int u = lane; u < units; u += 32) {
+        const uint4 v = ldg_cg_u4(p + 8 * u);
+        *reinterpret_cast<uint4*>(dst + stage_unit_offset<WT>(8 * u)) = v;
+      }
+      if (lane == 0) unscale[r] = 1.f;
+    } else {
+      float m = 0.f;
+      for (int u = lane; u < units; u += 32) m = fmaxf(m, bf16x8_absmax(ldg_cg_u4(p + 8 * u)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const int e = stage_exponent(m);
+      for (int u = lane; u < units; u += 32) {
+        const uint4 v = ldg_cg_u4(p + 8 * u);
+        *reinterpret_cast<uint4*>(dst + stage_unit_offset<WT>(8 * u)) =
+            bf16x8_to_f16x8_scaled(v, e);
+      }
+      if (lane == 0) unscale[r] = pow2f(-e);
+    }
+  }
+}
+
+// Ring of S register stages holding the weight loads of upcoming work units.
+template <int CPW, int S>
+struct WeightRing {
+  uint4 va[S][CPW];
+  uint4 vb[S][CPW];
+  uint32_t sa[S][CPW];
+  uint32_t sb[S][CPW];
+};
+
+}  // namespace fnx

@@ -1,0 +1,201 @@
+/*
+ * fnx_gemv.h — C ABI of the B200 (sm_100a) weight-only quantized GEMV library.
+ *
+ * Drop-in boundary for the reference's decode/verify GEMV operators.  Every entry point
+ * takes raw device pointers, element strides and sizes, plus the CUDA stream to launch
+ * on; nothing here allocates device memory.  Scratch buffers are owned by the caller
+ * and described by fnx_workspace / fnx_moe_workspace (sizes from the *_bytes queries).
+ *
+ * Return codes: FNX_OK on success; FNX_EINVAL for an argument the reference would
+ * reject (its `assert`s and `ValueError`s); FNX_EUNSUPPORTED for a shape this build does
+ * not tile (the caller keeps its fallback, as the reference's `apply_into` returning
+ * None does); FNX_ECUDA when the launch itself failed.  fnx_last_error() describes the
+ * last failure of the calling thread.
+ *
+ * Reference interfaces replaced (paths inside the reference repository):
+ *   fnx_w8a16_gemv           kernels/sglang/srt/layers/quantization/w8a16_gemv.py:642-666
+ *                            (w8a16_gemv) and :826-847 (bf16_gemv, w_dtype FNX_W_BF16)
+ *   fnx_w8a16_gemv_silu_mul  w8a16_gemv.py:1009-1061 (w8a16_gemv_silu_mul)
+ *   fnx_w4a16_nvfp4_gemv     kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:342-401
+ *   fnx_moe_gemv             patches/sglang/series/0112-DG1-one-token-draft-MoE-as-a-W4A16-
+ *                            NVFP4-Triton-GEMV.patch:328-386 (draft_moe_gemv), generalised
+ *                            from one token to M <= 16
+ *   fnx_argmax_decode        greedy top-1 over the logits buffer (the consumer of
+ *                            patches/sglang/series/0032-...patch:188-215's lm_head output)
+ *   fnx_*_workspace_bytes    w8a16_gemv.py:325-395 (split-K scratch, prealloc) and
+ *                            0112-...patch:307-325 (make_workspace)
+ */
+#ifndef FNX_GEMV_H_
+#define FNX_GEMV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t; kept opaque so the header needs no CUDA include. */
+typedef void* fnx_stream_t;
+
+#define FNX_OK 0
+#define FNX_EINVAL 1
+#define FNX_ECUDA 2
+#define FNX_EUNSUPPORTED 3
+
+/* Weight element formats. */
+#define FNX_W_INT8 0      /* int8, exact in the fp16 A operand                  */
+#define FNX_W_FP8_E4M3 1  /* float8_e4m3fn (the reference's W8A16 weights)      */
+#define FNX_W_BF16 2      /* bf16 (bf16_gemv)                                   */
+#define FNX_W_NVFP4 3     /* packed e2m1 pairs + e4m3 block-16 scales           */
+
+/* Output scale formats: applied per output row after the k reduction. */
+#define FNX_SCALE_NONE 0
+#define FNX_SCALE_F32_SCALAR 1
+#define FNX_SCALE_F32_ROW 2
+#define FNX_SCALE_BF16_SCALAR 3
+#define FNX_SCALE_BF16_ROW 4
+
+/* Maximum tokens per call (the reference asserts M <= 16, w8a16_gemv.py:658). */
+#define FNX_MAX_M 16
+
+/* Split-K and argmax scratch of the dense GEMVs.  Counters and keys must be zero when
+ * first used; every launch leaves them zero again (self-resetting, graph-replay safe).
+ * Two launches that share one workspace must not run concurrently (the reference's
+ * scratch_slot rule, w8a16_gemv.py:337-345). */
+typedef struct fnx_workspace {
+  float* partials;                 /* split-K fp32 partials                       */
+  int64_t partial_floats;          /* capacity of `partials`                      */
+  unsigned int* counters;          /* split-K per-tile arrival counters            */
+  int64_t n_counters;
+  unsigned long long* argmax_keys; /* FNX_MAX_M keys                              */
+  unsigned int* argmax_count;      /* one CTA arrival counter                     */
+} fnx_workspace;
+
+/* Optional launch geometry override (NULL = built-in planner).  warps: warps sharing
+ * one 16-row tile; chunks_per_warp: 64-byte row chunks each warp streams per tile (1, 2
+ * or 4); groups: tiles in flight per CTA; ksplit: k splits across CTAs; grid: CTAs
+ * (0 = persistent, one wave). */
+typedef struct fnx_gemv_cfg {
+  int warps;
+  int chunks_per_warp;
+  int groups;
+  int ksplit;
+  int grid;
+} fnx_gemv_cfg;
+
+/* Planner used when cfg is NULL (exposed for tests and workspace sizing). */
+int fnx_plan_gemv(int M, int N, int K, int w_dtype, int fused_silu, int argmax,
+                  fnx_gemv_cfg* out);
+
+/* Workspace floats / counters a call with this plan needs. */
+int fnx_gemv_workspace_need(int M, int N, int K, int w_dtype, int fused_silu,
+                            const fnx_gemv_cfg* cfg, int64_t* partial_floats,
+                            int64_t* n_counters);
+
+/*
+ * y[m, n] = bf16( (sum_k w[n, k] * x[m, k]) * scale[n] )      m < M <= 16, n < N
+ *
+ * x: bf16 [M, K], row stride ldx elements (16-byte aligned rows).
+ * w: [N, K] of w_dtype (FNX_W_INT8 / FNX_W_FP8_E4M3 / FNX_W_BF16), row stride ldw BYTES.
+ * scale: per-row or scalar scale (scale_kind), bf16 scales are widened exactly.
+ * y: [M, N] (or columns [0, split_n) when y2 != NULL), row stride ldy elements;
+ *    out_f32 != 0 stores the bf16-rounded value widened to fp32 (bit-identical to a bf16
+ *    result followed by a copy into an fp32 buffer, w8a16_gemv.py:599-618).
+ * y2: columns [split_n, N) at column n - split_n (two-destination store), or NULL.
+ * argmax_out: int64 [M] greedy top-1 row of the bf16-rounded logits (lowest row on
+ *    ties), or NULL.  row_offset is added to the row ids (vocab shards);
+ *    argmax_key_out (uint64 [M], may be NULL) receives the raw keys for a cross-shard
+ *    MAX reduction followed by fnx_argmax_decode.
+ */
+int fnx_w8a16_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, int w_dtype,
+                   const void* scale, int scale_kind, void* y, int64_t ldy, void* y2,
+                   int64_t ldy2, int64_t split_n, int out_f32, int64_t* argmax_out,
+                   unsigned long long* argmax_key_out, int64_t row_offset, int M, int N,
+                   int K, const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                   fnx_stream_t stream);
+
+/*
+ * y[m, j] = bf16( silu(g) * u ),  g = x_m . w[j] * scale[j],  u = x_m . w[H + j] * scale[H + j]
+ * w: [2H, K] with the gate half first (MergedColumnParallelLinear [gate|up]); scale per
+ * row (2H entries).  y: bf16 [M, H].
+ */
+int fnx_w8a16_gemv_silu_mul(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                            int w_dtype, const void* scale, int scale_kind, void* y,
+                            int64_t ldy, int M, int H, int K, const fnx_gemv_cfg* cfg,
+                            const fnx_workspace* ws, int pdl, fnx_stream_t stream);
+
+/*
+ * y[m, n] = bf16( (sum_k e2m1(wq[n, k]) * e4m3(bs[n, k / 16]) * x[m, k]) * gscale )
+ * wq: uint8 [N, K/2], low nibble = even k, row stride ldwq bytes.
+ * bs: e4m3 bytes [N, K/16] (linear layout), row stride ldbs bytes.
+ * gscale: fp32 scalar (gscale_per_row == 0) or [N]; the plain global scale (no 2^14
+ * factor: this library decodes e2m1 natively).
+ * Remaining arguments as fnx_w8a16_gemv.
+ */
+int fnx_w4a16_nvfp4_gemv(const void* x, int64_t ldx, const void* wq, int64_t ldwq,
+                         const void* bs, int64_t ldbs, const float* gscale,
+                         int gscale_per_row, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                         int64_t split_n, int out_f32, int64_t* argmax_out,
+                         unsigned long long* argmax_key_out, int64_t row_offset, int M,
+                         int N, int K, const fnx_gemv_cfg* cfg, const fnx_workspace* ws,
+                         int pdl, fnx_stream_t stream);
+
+/* NVFP4 expert bank in the server layout (ModelOptNvFp4FusedMoEMethod after
+ * process_weights_after_loading, 0112-...patch:68-76). */
+typedef struct fnx_moe_weights {
+  const void* w13;          /* uint8 [E, 2I, H/2]: rows [up(I); gate(I)]               */
+  const void* w13_scale;    /* e4m3 [E, 2I, H/16], 128x4 swizzled if scales_swizzled    */
+  const float* w13_gscale;  /* global scale of expert e at w13_gscale[e * stride]      */
+  int64_t w13_gscale_stride;
+  const void* w2;           /* uint8 [E, H, I/2]                                        */
+  const void* w2_scale;     /* e4m3 [E, H, I/16]                                        */
+  const float* w2_gscale;
+  int64_t w2_gscale_stride;
+  int num_experts;          /* experts held by these tensors                           */
+  int expert_offset;        /* global id of local expert 0 (expert-parallel shards)    */
+  int hidden;               /* H */
+  int inter;                /* I */
+  int scales_swizzled;
+} fnx_moe_weights;
+
+typedef struct fnx_moe_workspace {
+  void* act;             /* bf16 [M * (R + 1), I]                 */
+  float* partials;       /* fp32 [M * (R + 1), H]                 */
+  unsigned int* counters;/* [H / 16], zero when first used         */
+  int max_m;             /* capacity the buffers were sized for    */
+  int max_routes;
+} fnx_moe_workspace;
+
+/* Bytes of each fnx_moe_workspace buffer for (M, R, H, I). */
+int fnx_moe_workspace_bytes(int M, int R, int H, int I, int64_t* act_bytes,
+                            int64_t* partial_bytes, int64_t* counter_bytes);
+
+/*
+ * out[t, :] = sum_r topk_weights[t, r] * expert(topk_ids[t, r])(x[t]) [+ shared(x[t])]
+ * expert(x) = w2 @ (silu(gate(x)) * up(x)); act rounded to bf16 between the GEMVs.
+ * x: bf16 [M, H] (row stride ldx); topk_ids int32 [M, R] (ids < 0 skipped);
+ * topk_weights fp32 [M, R]; shared: an always-on expert with weight 1.0 (num_experts 1),
+ * or NULL.  out: bf16 [M, H] (row stride ldo), or the fp32 partial sum of this expert
+ * slice when out_f32 != 0 (for a cross-rank SUM).
+ */
+int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
+                 const float* topk_weights, int M, int R, const fnx_moe_weights* experts,
+                 const fnx_moe_weights* shared, void* out, int64_t ldo, int out_f32,
+                 const fnx_moe_workspace* ws, int pdl, fnx_stream_t stream);
+
+/* out[t] = row id encoded in keys[t] (after a cross-shard MAX reduction of the keys). */
+int fnx_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
+                      fnx_stream_t stream);
+
+/* Description of the last error of the calling thread ("" if none). */
+const char* fnx_last_error(void);
+
+/* Library version string. */
+const char* fnx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FNX_GEMV_H_ */

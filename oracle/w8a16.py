@@ -1,0 +1,84 @@
+"""W8A16 GEMV, fused gate_up SiLU and greedy argmax, restated in numpy (test oracle).
+
+Semantics (kernels/sglang/srt/layers/quantization/w8a16_gemv.py):
+* y[m, n] = (sum_k w[n, k] * x[m, k]) * s[n]; one-byte weights (fp8 e4m3 or int8) are
+  widened exactly; the scale is applied once per output after the k sum (:266-270); the
+  result is rounded to bf16 and only then widened when the destination is fp32 (:92-95).
+* scales: [N], [N, 1] or a scalar, fp32 or bf16 (the host upcasts to fp32, :660-662).
+* fused gate_up: silu(g) * u with g = x.w[j] * s[j], u = x.w[H + j] * s[H + j], the
+  activation evaluated on the unrounded fp32 values (:1009-1018, :930-935).
+* greedy argmax over the bf16-rounded logits, lowest index on ties (torch.argmax).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .numerics import bf16_round, bf16_round_from_f64, e4m3_to_f32
+
+
+def weight_values(w: np.ndarray, kind: str) -> np.ndarray:
+    """Exact fp64 values of a weight stored as 'int8', 'fp8' (e4m3 bytes) or 'bf16' (fp32 values)."""
+    if kind == "int8":
+        return np.asarray(w, dtype=np.int8).astype(np.float64)
+    if kind == "fp8":
+        return e4m3_to_f32(np.asarray(w, dtype=np.uint8)).astype(np.float64)
+    if kind == "bf16":
+        return np.asarray(w, dtype=np.float64)
+    raise ValueError(kind)
+
+
+def gemv_f64(x_bf16: np.ndarray, w: np.ndarray, kind: str, scale,
+             row_chunk: int = 16384) -> np.ndarray:
+    """Unrounded fp64 logits (x @ w^T) * s (rows in chunks to bound memory)."""
+    x = np.asarray(x_bf16, dtype=np.float64)
+    s = np.asarray(scale, dtype=np.float64).reshape(-1)
+    N = np.asarray(w).shape[0]
+    y = np.empty((x.shape[0], N), dtype=np.float64)
+    for r0 in range(0, N, row_chunk):
+        r1 = min(N, r0 + row_chunk)
+        y[:, r0:r1] = x @ weight_values(w[r0:r1], kind).T
+    return y * (s[None, :] if s.size > 1 else s[0])
+
+
+def gemv(x_bf16: np.ndarray, w: np.ndarray, kind: str, scale) -> np.ndarray:
+    """bf16-rounded logits (as fp32 values)."""
+    return bf16_round_from_f64(gemv_f64(x_bf16, w, kind, scale))
+
+
+def argmax_lowest(logits: np.ndarray) -> np.ndarray:
+    """Row-wise argmax, lowest index among equal maxima (torch.argmax semantics)."""
+    logits = np.asarray(logits)
+    return np.argmax(logits, axis=-1).astype(np.int64)  # numpy also returns the first max
+
+
+def top2_gap(logits_f64: np.ndarray) -> np.ndarray:
+    """Gap between the largest and second-largest exact logit of each row."""
+    part = np.partition(np.asarray(logits_f64, dtype=np.float64), -2, axis=-1)
+    return part[..., -1] - part[..., -2]
+
+
+def silu_mul(x_bf16: np.ndarray, w: np.ndarray, kind: str, scale) -> np.ndarray:
+    """bf16(silu(g) * u) of the fused gate_up form, evaluated in fp64."""
+    y = gemv_f64(x_bf16, w, kind, scale)
+    h = y.shape[1] // 2
+    g, u = y[:, :h], y[:, h:]
+    return bf16_round_from_f64(g / (1.0 + np.exp(-g)) * u)
+
+
+def silu_mul_two_step(x_bf16: np.ndarray, w: np.ndarray, kind: str, scale) -> np.ndarray:
+    """The unfused reference path: bf16 gate_up, then act_and_mul in fp32 -> bf16."""
+    y = gemv(x_bf16, w, kind, scale).astype(np.float32)
+    h = y.shape[1] // 2
+    g, u = y[:, :h], y[:, h:]
+    return bf16_round((g / (np.float32(1) + np.exp(-g))) * u)
+
+
+def reference_cpu_path(x: np.ndarray, w: np.ndarray, kind: str, scale):
+    """The reference's torch CPU path in fp32, restated: W = w.float() * s[:, None];
+    logits = bf16(x.float() @ W^T); token = argmax (used as the timed CPU baseline)."""
+    wf = weight_values(w, kind).astype(np.float32) if kind != "int8" else np.asarray(w, np.float32)
+    s = np.asarray(scale, dtype=np.float32).reshape(-1)
+    W = wf * (s[:, None] if s.size > 1 else s[0])
+    logits = bf16_round(np.asarray(x, dtype=np.float32) @ W.T)
+    return logits, argmax_lowest(logits)

@@ -1,0 +1,101 @@
+"""The C-ABI library on a machine without a GPU: it loads, exports every entry point
+include/fnx_gemv.h declares, plans every benchmark shape sensibly, and rejects invalid
+arguments (the reference's asserts / ValueErrors) before any launch."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from flash_next_rtxpro6000_b200 import _lib
+from flash_next_rtxpro6000_b200._lib import FnxGemvCfg, FnxMoeWeights, FnxMoeWorkspace
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "fnx_gemv.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(fnx_\w+)\(", src, re.M)))
+
+
+def test_header_declares_the_binding_surface():
+    assert declared() == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert lib.fnx_version().decode().startswith("fnx-b200")
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+@pytest.mark.parametrize("N,K,wt", [
+    (151936, 2048, _lib.W_INT8), (49152, 2048, _lib.W_INT8), (4096, 2048, _lib.W_NVFP4),
+    (1024, 2048, _lib.W_FP8_E4M3), (2048, 512, _lib.W_INT8), (1000, 2560, _lib.W_FP8_E4M3),
+    (32768, 2048, _lib.W_NVFP4), (700, 1024, _lib.W_BF16)])
+def test_planner_invariants(M, N, K, wt):
+    c = FnxGemvCfg()
+    assert _lib.lib().fnx_plan_gemv(M, N, K, wt, 0, 0, ctypes.byref(c)) == 0
+    ch = {_lib.W_INT8: 64, _lib.W_FP8_E4M3: 64, _lib.W_BF16: 32, _lib.W_NVFP4: 128}[wt]
+    assert c.warps * c.chunks_per_warp * c.ksplit == K // ch
+    assert c.warps * 32 >= 16 * M
+    assert 1 <= c.groups <= 8 and c.warps * c.groups <= 16
+    assert c.chunks_per_warp in (1, 2, 4)
+    if N >= 49152:
+        assert c.ksplit == 1  # the wide heads fill the machine on N alone
+
+
+def _gemv(**kw):
+    args = dict(x=16, ldx=2048, w=16, ldw=2048, wt=_lib.W_INT8, s=16, sk=_lib.SCALE_F32_ROW,
+                y=16, ldy=1024, y2=None, ldy2=0, split=0, f32=0, am=None, key=None, off=0,
+                M=1, N=1024, K=2048, cfg=None, ws=None, pdl=0, stream=None)
+    args.update(kw)
+    return _lib.lib().fnx_w8a16_gemv(*args.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(M=17), _lib.FNX_EINVAL),
+    (dict(x=None), _lib.FNX_EINVAL),
+    (dict(x=8), _lib.FNX_EINVAL),               # misaligned activation rows
+    (dict(ldw=2040), _lib.FNX_EINVAL),          # row stride below K / not 16-byte
+    (dict(K=2000, ldx=2000, ldw=2000), _lib.FNX_EUNSUPPORTED),
+    (dict(K=2016, ldx=2016, ldw=2016), _lib.FNX_EUNSUPPORTED),
+    (dict(sk=9), _lib.FNX_EINVAL),
+    (dict(y2=16, ldy2=1024, split=0), _lib.FNX_EINVAL),
+    (dict(y2=16, ldy2=1024, split=1024), _lib.FNX_EINVAL),
+    (dict(am=16), _lib.FNX_EINVAL),             # argmax without a workspace
+    (dict(wt=_lib.W_NVFP4), _lib.FNX_EINVAL),   # NVFP4 has its own entry point
+])
+def test_invalid_arguments_are_rejected(kw, code):
+    assert _gemv(**kw) == code
+    assert _lib.last_error()
+
+
+def test_zero_tokens_returns_ok_without_launch():
+    assert _gemv(M=0) == _lib.FNX_OK
+
+
+def test_moe_validation():
+    lib = _lib.lib()
+    w = FnxMoeWeights(16, 16, 16, 2, 16, 16, 16, 1, 512, 0, 2000, 512, 1)
+    ws = FnxMoeWorkspace(16, 16, 16, 16, 10)
+    rc = lib.fnx_moe_gemv(16, 2000, 16, 16, 1, 10, ctypes.byref(w), None, 16, 2000, 0,
+                          ctypes.byref(ws), 0, None)
+    assert rc == _lib.FNX_EUNSUPPORTED
+    w.hidden = 2048
+    rc = lib.fnx_moe_gemv(16, 2048, 16, 16, 17, 10, ctypes.byref(w), None, 16, 2048, 0,
+                          ctypes.byref(ws), 0, None)
+    assert rc == _lib.FNX_EINVAL
+    ws.max_m = 1
+    rc = lib.fnx_moe_gemv(16, 2048, 16, 16, 2, 10, ctypes.byref(w), None, 16, 2048, 0,
+                          ctypes.byref(ws), 0, None)
+    assert rc == _lib.FNX_EINVAL
+
+
+def test_moe_workspace_bytes():
+    a, p, c = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    assert _lib.lib().fnx_moe_workspace_bytes(16, 10, 2048, 512, ctypes.byref(a), ctypes.byref(p),
+                                              ctypes.byref(c)) == 0
+    assert (a.value, p.value, c.value) == (16 * 11 * 512 * 2, 16 * 11 * 2048 * 4, 128 * 4)

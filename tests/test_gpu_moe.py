@@ -1,0 +1,199 @@
+"""Routed NVFP4 MoE (config 2) on the GPU against the CPU oracle.
+
+Checks, after the reference's own (bench/bench/dg1/dg1_bench.py correctness and
+determinism phases, bench/bench/dg1/selftest_cpu.py): output within 2e-2 of the
+dequantise-then-matmul layer (with and without the bf16 rounding of the activation
+between the two GEMVs), ids < 0 skipped, bitwise reruns, counters back at zero,
+graph replay on new inputs, the 128x4 swizzled and linear scale layouts agree, and
+expert-sliced partial sums add up to the whole layer."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as omoe, nvfp4 as onv
+from tests.gpu_util import REL_TOL, dev, rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+
+_LAYERS = {}
+
+
+def _layer(E, H=2048, I=512, seed=0):
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    key = (E, H, I, seed)
+    if key not in _LAYERS:
+        L = syn.moe_layer(E, H, I, seed=seed)
+        sw13 = onv.swizzle_blockscale(L.s13.numpy())
+        sw2 = onv.swizzle_blockscale(L.s2.numpy())
+        ssw13 = onv.swizzle_blockscale(L.sh_s13.numpy())
+        ssw2 = onv.swizzle_blockscale(L.sh_s2.numpy())
+        d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev()) for k, v in dict(
+            w13=L.w13.numpy(), s13=sw13, g13=L.g13.numpy(), w2=L.w2.numpy(), s2=sw2,
+            g2=L.g2.numpy(), sh_w13=L.sh_w13.numpy(), sh_s13=ssw13, sh_g13=L.sh_g13.numpy(),
+            sh_w2=L.sh_w2.numpy(), sh_s2=ssw2, sh_g2=L.sh_g2.numpy(),
+            s13_lin=L.s13.numpy(), s2_lin=L.s2.numpy(), sh_s13_lin=L.sh_s13.numpy(),
+            sh_s2_lin=L.sh_s2.numpy()).items()}
+        _LAYERS[key] = (L, d)
+    return _LAYERS[key]
+
+
+def _shared(fx, d, linear=False):
+    sfx = "_lin" if linear else ""
+    return fx.SharedExpert(d["sh_w13"], d["sh_s13" + sfx], d["sh_g13"], d["sh_w2"],
+                           d["sh_s2" + sfx], d["sh_g2"])
+
+
+def _run(fx, d, x, ids, wts, ws, shared=True, linear=False, **kw):
+    sfx = "_lin" if linear else ""
+    return fx.draft_moe_gemv(
+        hidden_states=x, topk_ids=ids, topk_weights=wts, w13_weight=d["w13"],
+        w13_blockscale_swizzled=d["s13" + sfx], w13_weight_scale_2=d["g13"], w2_weight=d["w2"],
+        w2_blockscale_swizzled=d["s2" + sfx], w2_weight_scale_2=d["g2"], workspace=ws,
+        shared_expert=_shared(fx, d, linear) if shared else None, scales_swizzled=not linear, **kw)
+
+
+def _oracle(L, x, ids, wts, shared=True, act_round=True, **kw):
+    sh = None
+    if shared:
+        sh = dict(w13=L.sh_w13.numpy()[0], s13=L.sh_s13.numpy()[0], g13=L.sh_g13.numpy(),
+                  w2=L.sh_w2.numpy()[0], s2=L.sh_s2.numpy()[0], g2=L.sh_g2.numpy())
+    return omoe.moe(x.float().numpy(), ids.numpy(), wts.numpy(), L.w13.numpy(), L.s13.numpy(),
+                    L.g13.numpy(), L.w2.numpy(), L.s2.numpy(), L.g2.numpy(), shared=sh,
+                    order="server", act_round=act_round, **kw)
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
+def test_config2_matches_oracle(M):
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    E = 512 if M in (1, 16) else 64
+    L, d = _layer(E)
+    x = syn.activations(M, seed=5)
+    ids, wts = syn.routing(M, E=E, seed=M)
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    y = _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws)
+    torch.cuda.synchronize()
+    got = to_np(y)
+    ref = _oracle(L, x, ids, wts)                 # act rounded to bf16 (the kernel's arithmetic)
+    ref_dq = _oracle(L, x, ids, wts, act_round=False)
+    assert y.shape == (M, 2048) and y.dtype == torch.bfloat16
+    assert rel_err(got, ref) <= REL_TOL
+    assert rel_err(got, ref_dq) <= REL_TOL
+    l2 = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert l2 < 5e-3, l2
+    assert int(ws.counters.abs().sum()) == 0
+
+
+def test_negative_ids_are_skipped_and_no_shared():
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(64)
+    M = 3
+    x = syn.activations(M, seed=6)
+    ids, wts = syn.routing(M, E=64, seed=6)
+    ids[1, 3] = -1
+    ids[1, 7] = -1
+    ids[2, :] = -1
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    y = _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws, shared=False)
+    ref = _oracle(L, x, ids, wts, shared=False)
+    got = to_np(y)
+    assert np.all(got[2] == 0)
+    assert rel_err(got[:2], ref[:2]) <= REL_TOL
+
+
+@pytest.mark.parametrize("M", [1, 16])
+def test_deterministic_and_graph_replay(M):
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(512)
+    x = syn.activations(M, seed=7).to(dev())
+    ids, wts = syn.routing(M, E=512, seed=70 + M)
+    ids, wts = ids.to(dev()), wts.to(dev())
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    a = _run(fx, d, x, ids, wts, ws).clone()
+    b = _run(fx, d, x, ids, wts, ws).clone()
+    assert torch.equal(a, b)
+    # linear (unswizzled) scale layout gives the same bits
+    c = _run(fx, d, x, ids, wts, ws, linear=True)
+    assert torch.equal(a, c)
+    xs, is_, ws_ = x.clone(), ids.clone(), wts.clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            _run(fx, d, xs, is_, ws_, ws)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        yg = _run(fx, d, xs, is_, ws_, ws)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(yg, a)
+    x2 = syn.activations(M, seed=8)
+    ids2, wts2 = syn.routing(M, E=512, seed=80 + M)
+    xs.copy_(x2.to(dev()))
+    is_.copy_(ids2.to(dev()))
+    ws_.copy_(wts2.to(dev()))
+    g.replay()
+    torch.cuda.synchronize()
+    ref2 = _oracle(L, x2, ids2, wts2)
+    assert rel_err(to_np(yg), ref2) <= REL_TOL
+    assert int(ws.counters.abs().sum()) == 0
+    del g
+
+
+def test_expert_slices_sum_to_layer():
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(64)
+    M = 16
+    x = syn.activations(M, seed=9).to(dev())
+    ids, wts = syn.routing(M, E=64, seed=9)
+    ids, wts = ids.to(dev()), wts.to(dev())
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    full = _run(fx, d, x, ids, wts, ws, out_f32=True)
+    total = torch.zeros_like(full)
+    G = 4
+    per = 64 // G
+    for r in range(G):
+        sl = slice(r * per, (r + 1) * per)
+        part = fx.draft_moe_gemv(
+            hidden_states=x, topk_ids=ids, topk_weights=wts, w13_weight=d["w13"][sl].contiguous(),
+            w13_blockscale_swizzled=d["s13"][sl].contiguous(), w13_weight_scale_2=d["g13"][sl].contiguous(),
+            w2_weight=d["w2"][sl].contiguous(), w2_blockscale_swizzled=d["s2"][sl].contiguous(),
+            w2_weight_scale_2=d["g2"][sl].contiguous(), workspace=ws,
+            shared_expert=_shared(fx, d) if r == 0 else None, expert_offset=r * per, out_f32=True)
+        total += part
+    assert rel_err(to_np(total), to_np(full)) <= 1e-5
+
+
+def test_runner_maybe_apply_and_capture_guard():
+    import types
+
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(64)
+    layer = types.SimpleNamespace(layer_id=0, w13_weight=d["w13"], w13_blockscale_swizzled=d["s13"],
+                                  w13_weight_scale_2=d["g13"], w2_weight=d["w2"],
+                                  w2_blockscale_swizzled=d["s2"], w2_weight_scale_2=d["g2"])
+    x = syn.activations(2, seed=4).to(dev())
+    ids, wts = syn.routing(2, E=64, seed=4)
+    disp = types.SimpleNamespace(hidden_states=x, hidden_states_scale=None,
+                                 topk_output=types.SimpleNamespace(topk_ids=ids.to(dev()),
+                                                                   topk_weights=wts.to(dev())))
+    runner = fx.DraftMoeGemvRunner()
+    out = runner.maybe_apply(layer=layer, dispatch_output=disp)
+    ref = _oracle(L, x.cpu(), ids, wts, shared=False)
+    assert rel_err(to_np(out.hidden_states), ref) <= REL_TOL
+    big = types.SimpleNamespace(hidden_states=torch.zeros(17, 2048, dtype=torch.bfloat16, device=dev()),
+                                hidden_states_scale=None, topk_output=disp.topk_output)
+    assert runner.maybe_apply(layer=layer, dispatch_output=big) is None

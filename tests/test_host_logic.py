@@ -1,0 +1,127 @@
+"""Host-side logic that needs no GPU: destination validation (w8a16_gemv.py:599-639),
+scratch slots, MoE shape gating (0112-...patch:289-305), argmax key encoding, the
+synthetic generators' byte model, and the multi-rank exchange of the sharded head and
+the expert-sharded MoE on 2 gloo ranks."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import importlib
+
+from flash_next_rtxpro6000_b200 import sharded, synthetic
+from oracle import numerics
+
+# the package re-exports functions under the module names; take the modules themselves
+dmg = importlib.import_module("flash_next_rtxpro6000_b200.draft_moe_gemv")
+w8 = importlib.import_module("flash_next_rtxpro6000_b200.w8a16_gemv")
+
+
+def test_out_validation():
+    d = torch.device("cpu")
+    assert w8._out_or_new(None, 2, 8, d).shape == (2, 8)
+    good = torch.empty(2, 8, dtype=torch.float32)
+    assert w8._out_or_new(good, 2, 8, d) is good
+    for bad in (torch.empty(2, 9), torch.empty(2, 8, dtype=torch.float16), torch.empty(8, 2).t()):
+        with pytest.raises(ValueError):
+            w8._out_or_new(bad, 2, 8, d)
+    with pytest.raises(ValueError):
+        w8._split_dests(None, torch.empty(2, 3), 0, 2, 8, d)
+    y, y2, s = w8._split_dests(None, None, 0, 2, 8, d)
+    assert y2 is None and s == 0
+
+
+def test_scratch_slot_nesting():
+    assert w8._SLOT == 0
+    with w8.scratch_slot(1):
+        assert w8._SLOT == 1
+        with w8.scratch_slot(0):
+            assert w8._SLOT == 0
+        assert w8._SLOT == 1
+    assert w8._SLOT == 0
+
+
+def test_unsupported_reason():
+    assert dmg.unsupported_reason(hidden_size=2048, intermediate_size=512) is None
+    assert dmg.unsupported_reason(hidden_size=2560, intermediate_size=640) is None
+    assert "multiples of 128" in dmg.unsupported_reason(hidden_size=2000, intermediate_size=512)
+    assert dmg.unsupported_reason(hidden_size=8192, intermediate_size=512) is not None
+
+
+def test_argmax_key_orders_like_torch_argmax():
+    rng = np.random.default_rng(0)
+    v = numerics.bf16_round(rng.standard_normal(4000).astype(np.float32) * 4)
+    v[[10, 200, 3000]] = v.max()  # ties: lowest row must win
+    v[5] = -0.0
+    bits = numerics.bf16_bits(v)
+    keys = [sharded.encode_key(int(b), i) for i, b in enumerate(bits)]
+    assert sharded.decode_key(max(keys)) == int(np.argmax(v)) == 10
+    zero = [sharded.encode_key(0x8000, 0), sharded.encode_key(0x0000, 1)]
+    assert sharded.decode_key(max(zero)) == 0  # -0 == +0 ties -> lowest row
+
+
+def test_byte_model_matches_survey_figures():
+    assert synthetic.w8_head_bytes(151936, 2048, 1, argmax=False) == 311_776_768
+    assert synthetic.w8_head_bytes(49152, 2048, 1, argmax=False) == 100_864_000
+    assert synthetic.nvfp4_bytes(4096, 2048, 1) == 4_730_880
+    assert synthetic.moe_bytes(10, M=1) == 19_472_384
+
+
+def test_routing_generator():
+    ids, w = synthetic.routing(16, seed=0)
+    assert ids.shape == (16, 10) and ids.dtype == torch.int32
+    assert torch.allclose(w.sum(-1), torch.ones(16))
+    for row in ids:
+        assert len(set(row.tolist())) == 10
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(1)
+        V, M = 4096, 3
+        logits = numerics.bf16_round(rng.standard_normal((M, V)).astype(np.float32) * 3)
+        logits[1, 17] = logits[1, 3000] = logits[1].max() + 1  # tie across the two shards
+        r0, n = sharded.shard_rows(V, world, rank)
+        bits = numerics.bf16_bits(logits[:, r0:r0 + n])
+        keys = torch.tensor([max(sharded.encode_key(int(b), r0 + j) for j, b in enumerate(row))
+                             for row in bits], dtype=torch.int64)
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+        got = [sharded.decode_key(int(k)) for k in keys]
+        # expert-sharded partial sums
+        part = torch.full((2, 4), float(rank + 1))
+        dist.all_reduce(part, op=dist.ReduceOp.SUM)
+        q.put((rank, got, np.argmax(logits, axis=-1).tolist(), float(part[0, 0])))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_exchange_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got, want, s in res:
+        assert got == want
+        assert want[1] == 17
+        assert s == 3.0
