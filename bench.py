@@ -271,6 +271,8 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
     import torch
     import torch.distributed as dist
 
+    from flash_next_rtxpro6000_b200 import _lib
+
     Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
     V = syn.VOCAB if args.workload == "lm_head" else syn.DRAFT_VOCAB
     K = syn.HIDDEN
@@ -400,45 +402,71 @@ def e2e_lm_head(args, fx, syn, dev, w, s, Ms, world, rank, r0, shard, V, K):
             "d2h_bytes_per_step": sum(m * 8 for m in Ms), "steps": steps}
 
 
+def _graph_of(calls, warm=3):
+    """Capture a list of zero-argument launches into one CUDA graph (after warm-up)."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warm):
+            for c in calls:
+                c()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for c in calls:
+            c()
+    torch.cuda.synchronize()
+    return g
+
+
 def bench_nvfp4(args, fx, syn, dev):
-    """Config 0 (NVFP4 4096 x 2048): 64 weight copies rotated (> 4x L2)."""
+    """Config 0 (NVFP4 4096 x 2048): 64 weight copies rotated (> 4x L2) inside one CUDA
+    graph, so the timing is device time, not Python dispatch."""
     import torch
 
     Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
     copies = 64
     ws = [syn.nvfp4_weight(syn.NVFP4_N, syn.HIDDEN, seed=i) for i in range(copies)]
     ws = [(w.wq.to(dev), w.bs.to(dev), w.gscale.to(dev)) for w in ws]
-    xs = [syn.activations(m, seed=1).to(dev) for m in Ms]
-    ys = [torch.empty(m, syn.NVFP4_N, dtype=torch.bfloat16, device=dev) for m in Ms]
-    it = [0]
-
-    def step():
-        for i, x in enumerate(xs):
-            wq, bs, g = ws[it[0] % copies]
-            it[0] += 1
-            fx.w4a16_nvfp4_gemv(x, wq, bs, g, out=ys[i], pdl=True)
-
-    sampler = ClockSampler(_gpu_id(dev))
-    ms, clocks = _timed(step, args.steps, max(3, args.warmup), dev, 1, sampler)
-    per_step = sum(syn.nvfp4_bytes(syn.NVFP4_N, syn.HIDDEN, m) for m in Ms)
-    value = per_step * args.steps / (ms / 1e3) / 1e9
     peak, src = measured_peak()
+    per_m, total_bytes, total_ms = {}, 0, 0.0
+    sampler = ClockSampler(_gpu_id(dev))
+    clocks = None
+    for M in Ms:
+        x = syn.activations(M, seed=1).to(dev)
+        y = torch.empty(M, syn.NVFP4_N, dtype=torch.bfloat16, device=dev)
+        calls = [(lambda w=w: fx.w4a16_nvfp4_gemv(x, w[0], w[1], w[2], out=y, pdl=True))
+                 for w in ws]
+        g = _graph_of(calls)
+        reps = max(3, args.steps // copies)
+        ms, ck = _timed(g.replay, reps, max(3, args.warmup // copies), dev, 1,
+                        sampler if M == Ms[-1] else None)
+        clocks = ck or clocks
+        us = ms / (reps * copies) * 1e3
+        b = syn.nvfp4_bytes(syn.NVFP4_N, syn.HIDDEN, M)
+        per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1)}
+        total_bytes += b * reps * copies
+        total_ms += ms
+        del g
+    value = total_bytes / (total_ms / 1e3) / 1e9
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": "nvfp4_gemv_4096x2048", "M": Ms,
-                       "l2": f"{copies} weight copies rotated (> 4x L2)"},
-            "us_per_call": round(ms / args.steps / len(Ms) * 1e3, 3),
+                       "l2": f"{copies} weight copies rotated in one CUDA graph (> 4x L2)"},
+            "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": args.steps * len(Ms)}
+            "clocks": clocks, "gpu_launches": None}
 
 
 def bench_moe(args, fx, syn, dev):
-    """Config 2 (NVFP4 MoE, 512 experts, top-10 + shared expert).  Routings rotate over
-    disjoint expert sets so the weights come from HBM (> 4x L2 across the rotation)."""
-    import numpy as np
+    """Config 2 (NVFP4 MoE, 512 experts, top-10 + shared expert).  48 routings rotate over
+    shifted expert sets (> 4x L2 across the rotation) inside one CUDA graph."""
     import torch
 
     from flash_next_rtxpro6000_b200.w4a16_nvfp4_gemv import swizzle_blockscale
@@ -456,52 +484,51 @@ def bench_moe(args, fx, syn, dev):
     peak, src = measured_peak()
     total_bytes, total_ms = 0, 0.0
     sampler = ClockSampler(_gpu_id(dev))
+    clocks = None
+    n_rot = 48
     for M in Ms:
-        n_rot = 48
-        rots = []
-        nbytes = 0
+        rots, nbytes = [], 0
         for r in range(n_rot):
             ids, wts = syn.routing(M, E=syn.EXPERTS, seed=1000 * M + r)
-            # shift expert ids by a rotation-dependent offset: successive calls touch
-            # different experts, as consecutive decode layers do
+            # shift the expert ids per rotation: successive calls touch different experts,
+            # as consecutive decode layers do
             ids = ((ids.long() + 97 * r) % syn.EXPERTS).to(torch.int32)
-            D = int(torch.unique(ids).numel())
-            nbytes += syn.moe_bytes(D, M=M)
+            nbytes += syn.moe_bytes(int(torch.unique(ids).numel()), M=M)
             rots.append((ids.to(dev), wts.to(dev)))
         x = syn.activations(M, seed=3).to(dev)
         out = torch.empty(M, syn.HIDDEN, dtype=torch.bfloat16, device=dev)
-        it = [0]
 
-        def step():
-            ids, wts = rots[it[0] % n_rot]
-            it[0] += 1
+        def call(ids, wts):
             fx.draft_moe_gemv(hidden_states=x, topk_ids=ids, topk_weights=wts,
                               w13_weight=d["w13"], w13_blockscale_swizzled=d["s13"],
                               w13_weight_scale_2=d["g13"], w2_weight=d["w2"],
                               w2_blockscale_swizzled=d["s2"], w2_weight_scale_2=d["g2"],
-                              workspace=ws, shared_expert=shared, out=out)
+                              workspace=ws, shared_expert=shared, out=out,
+                              cfg=fx.DraftMoeGemvConfig(pdl=True))
 
-        steps = (args.steps // n_rot + 1) * n_rot
-        ms, clocks = _timed(step, steps, max(n_rot, args.warmup), dev, 1, sampler if M == Ms[-1] else None)
+        g = _graph_of([(lambda r=r: call(*r)) for r in rots])
+        reps = max(3, args.steps // n_rot)
+        ms, ck = _timed(g.replay, reps, 3, dev, 1, sampler if M == Ms[-1] else None)
+        clocks = ck or clocks
+        us = ms / (reps * n_rot) * 1e3
         bytes_per_call = nbytes / n_rot
-        us = ms / steps * 1e3
         results[str(M)] = {"us_per_call": round(us, 3),
                            "GBps": round(bytes_per_call / (us * 1e-6) / 1e9, 1),
                            "bytes_per_call": int(bytes_per_call)}
-        total_bytes += bytes_per_call * steps
+        total_bytes += bytes_per_call * reps * n_rot
         total_ms += ms
+        del g
     value = total_bytes / (total_ms / 1e3) / 1e9
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_ms / max(1, args.steps), 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/bf16 (fp32 accumulate)",
-            "data": "synthetic",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
-                       "l2": "48 routings over rotated expert sets (> 4x L2)"},
+                       "l2": f"{n_rot} routings over shifted expert sets in one CUDA graph (> 4x L2)"},
             "per_m": results,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": 2 * sum(1 for _ in Ms) * args.steps}
+            "clocks": clocks, "gpu_launches": None}
 
 
 if __name__ == "__main__":

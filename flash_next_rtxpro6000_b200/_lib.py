@@ -39,6 +39,7 @@ class FnxWorkspace(ctypes.Structure):
         ("n_counters", c_int64),
         ("argmax_keys", c_void_p),
         ("argmax_count", c_void_p),
+        ("error_flag", c_void_p),
     ]
 
 
@@ -73,10 +74,25 @@ class FnxMoeWeights(ctypes.Structure):
 class FnxMoeWorkspace(ctypes.Structure):
     _fields_ = [
         ("act", c_void_p),
+        ("act_f16", c_void_p),
+        ("pair_unscale", c_void_p),
+        ("expert_counters", c_void_p),
         ("partials", c_void_p),
         ("counters", c_void_p),
+        ("error_flag", c_void_p),
         ("max_m", c_int),
         ("max_routes", c_int),
+    ]
+
+
+class FnxMoeWorkspaceSizes(ctypes.Structure):
+    _fields_ = [
+        ("act", c_int64),
+        ("act_f16", c_int64),
+        ("pair_unscale", c_int64),
+        ("expert_counters", c_int64),
+        ("partials", c_int64),
+        ("counters", c_int64),
     ]
 
 
@@ -102,7 +118,8 @@ def _declare(lib):
         _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
         c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),
         POINTER(FnxWorkspace), c_int, _P]
-    lib.fnx_moe_workspace_bytes.argtypes = [c_int, c_int, c_int, c_int, _I64P, _I64P, _I64P]
+    lib.fnx_moe_workspace_bytes.argtypes = [c_int, c_int, c_int, c_int, c_int,
+                                            POINTER(FnxMoeWorkspaceSizes)]
     lib.fnx_moe_gemv.argtypes = [
         _P, c_int64, _P, _P, c_int, c_int, POINTER(FnxMoeWeights), POINTER(FnxMoeWeights), _P,
         c_int64, c_int, POINTER(FnxMoeWorkspace), c_int, _P]

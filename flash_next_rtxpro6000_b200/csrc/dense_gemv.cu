@@ -6,247 +6,436 @@
 //   _w4a16_nvfp4_gemv_kernel  kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:122-216
 // with one persistent sm_100a kernel family.
 //
-// Work decomposition.  A work unit is one 16-row weight tile (8 output columns of gate
-// plus the matching 8 of up for the fused SiLU form) over a k range; a group of W warps
-// shares the unit, each warp streaming CPW 64-byte chunks of every row with 128-bit
-// loads into a ring of S register stages, so S-1 units of loads are in flight while the
-// current one is multiplied.  The group's partial tiles are summed in shared memory in a
-// fixed order (deterministic), then scaled, rounded to bf16 (w8a16_gemv.py:92-95) and
-// stored.  With ksplit > 1 the k range is split across groups and the last group to
-// finish a tile sums the partials in split order and resets the tile counter
-// (w8a16_gemv.py:289-321), so no memset is needed between calls or graph replays.
+// Work decomposition.  A work unit is RT 16-row weight tiles (a SiLU tile is 8 gate rows
+// plus the matching 8 up rows) over the k range of one split.  Each persistent CTA runs
+// three roles:
+//   * warp 0, producer: one bulk copy (cp.async.bulk, mbarrier completion) per weight
+//     row into an NS-stage shared-memory ring, issued by the warp's lanes in parallel;
+//   * warps 2.., consumers: each takes one k slice of one row tile, reads its 64-byte
+//     chunks from the stage with conflict-free 128-bit loads, dequantises in registers
+//     and runs mma.sync on two independent accumulator chains; it then hands the
+//     partial tile to the epilogue through a double-buffered reduction slot;
+//   * warp 1, epilogue: sums the k slices in a fixed order, applies the per-token and
+//     per-row scales, rounds to bf16 (w8a16_gemv.py:92-95) and stores; with ksplit > 1
+//     it publishes the split's tile sums and the last split to arrive sums them in split
+//     order and resets the tile counter (w8a16_gemv.py:289-321).
+// Roles synchronise only through mbarriers (no CTA-wide barrier in the steady state) and
+// every wait is bounded (an expired wait records an error code and ends the role).
 //
-// Greedy argmax (fused).  Each output thread builds a 64-bit key of its bf16-rounded
-// logit and global row; the key maximum is the largest logit with the lowest row on
-// ties (torch.argmax).  Keys are reduced per tile with shuffles, per CTA in registers,
-// across CTAs with one atomicMax per token, and the last CTA decodes and clears them.
+// Greedy argmax (fused).  The epilogue builds a 64-bit key of each bf16-rounded logit
+// and its global row; the key maximum is the largest logit with the lowest row on ties
+// (torch.argmax).  Keys are reduced per tile with shuffles, per CTA in registers, across
+// CTAs with one atomicMax per token, and the last CTA decodes and clears them.
 #include "fnx_common.cuh"
 #include "fnx_kernels.h"
 
 namespace fnx {
 
-template <int WT, int NT, int CPW, int S>
-__global__ void __launch_bounds__(512, 1) dense_gemv_kernel(const DenseArgs a) {
+template <int WT, int NT, int CPW>
+__global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const DenseArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int Q = Geo<WT>::Q;
+  constexpr int kMaxRT = 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int W = a.W;
-  const int grp = warp / W, wig = warp - grp * W;
-  const int gthreads = W * 32, gtid = tid - grp * gthreads;
-  const int g = lane >> 2, c = lane & 3;
   const int M = a.M, N = a.N, K = a.K;
+  const int W = a.W, RT = a.RT, NS = a.NS, E = a.E, UB = a.UB, TILE = a.TILE;
+  const int RS = E;        // one reduction slot per epilogue warp
+  const int KSL = W / RT;  // consumer warps sharing one row tile (k slices)
+  const DenseStage SG = dense_stage(WT == W_NVFP4, RT, TILE, a.nch_u);
+  const DenseLayout L = dense_layout(M, K, W, NS, RS, NT, SG.bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + NS;
+  uint64_t* rfull = empty + NS;
+  uint64_t* rfree = rfull + RS;
+  uint8_t* stages = smem + L.stages;
+  uint8_t* xs = smem + L.xs;
+  float* unscale = reinterpret_cast<float*>(smem + L.unscale);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* sred = reinterpret_cast<float*>(smem + L.sred);
   const int srow = stage_row_bytes(K);
-
-  uint8_t* xs = smem;
-  float* unscale = reinterpret_cast<float*>(smem + (size_t)M * srow);
-  float* red = unscale + 16;  // [G][2][W][32][NT][4]
-  int* flags = reinterpret_cast<int*>(red + (size_t)a.G * 2 * W * 32 * NT * 4);
-
-  const uint64_t pol = policy_evict_first();
-  const int stride = gridDim.x * a.G;
-  const int first = blockIdx.x * a.G + grp;
-  const int n_units = a.n_units;
   const int ksplit = a.ksplit;
-  const int cpu = W * CPW;  // chunks per unit
+  const int n_units = a.n_units;
+  const int stride = gridDim.x;
+  const int first = blockIdx.x;
+  const int my_units = first < n_units ? (n_units - first + stride - 1) / stride : 0;
   const bool silu = a.silu != 0;
+  const bool per_row = a.scale_kind == SCALE_F32_ROW || a.scale_kind == SCALE_BF16_ROW;
+  const int esz = a.scale_kind == SCALE_BF16_ROW ? 2 : 4;
+  const int g = lane >> 2, c = lane & 3;
+  const int pg = phys_lo(g), pg8 = phys_hi(g);  // physical rows of MMA rows g, g + 8
 
-  // Weight row of MMA row i (0..15) of a tile; `ok` false for rows past the end (their
-  // loads are redirected to row 0 and their outputs dropped).
-  auto row_of = [&](int tile, int i, bool& ok) -> int {
-    if (silu) {
-      const int col = tile * 8 + (i & 7);
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1 + 32);  // bulk-copy arrival + one cp.async arrival per lane
+      mbar_init(&empty[s], W);
+    }
+    for (int r = 0; r < RS; ++r) {
+      mbar_init(&rfull[r], W);
+      mbar_init(&rfree[r], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  // Weight row of physical row r (0..15) of row tile t; rows past the end read row 0.
+  auto row_of = [&](int t, int r, bool& ok) -> int {
+    if (silu) {  // rows 0..7 gate, 8..15 up
+      const int col = t * 8 + (r & 7);
       ok = col < N;
-      return ok ? ((i < 8) ? col : N + col) : 0;
+      return ok ? ((r < 8) ? col : N + col) : 0;
     }
-    const int r = tile * 16 + i;
-    ok = r < N;
-    return ok ? r : 0;
+    const int n = t * 16 + r;
+    ok = n < N;
+    return ok ? n : 0;
+  };
+  auto whole_tile = [&](int t) { return silu ? (t * 8 + 7 < N) : (t * 16 + 15 < N); };
+  const bool contiguous = a.ldw == UB;  // a half tile is one block of 8 rows
+  // Row scales are staged when a full tile's 16 (or 2 x 8, SiLU) values are 16-byte
+  // aligned blocks; otherwise the consumer reads them from global memory.
+  auto staged_scales = [&](int t) {
+    if (!per_row || !whole_tile(t)) return false;
+    const uintptr_t base = reinterpret_cast<uintptr_t>(a.scale);
+    if (silu) return ((base + (size_t)t * 8 * esz) % 16 == 0) && ((base + ((size_t)N + t * 8) * esz) % 16 == 0);
+    return (base + (size_t)t * 16 * esz) % 16 == 0;
   };
 
-  WeightRing<CPW, S> ring;
-
-  auto load = [&](int u, uint4(&va)[CPW], uint4(&vb)[CPW], uint32_t(&sa)[CPW],
-                  uint32_t(&sb)[CPW]) {
-    const int tile = u / ksplit, ks = u - tile * ksplit;
-    bool oka, okb;
-    const int ra = row_of(tile, g, oka), rb = row_of(tile, g + 8, okb);
-    const uint8_t* pa = a.w + (size_t)ra * a.ldw;
-    const uint8_t* pb = a.w + (size_t)rb * a.ldw;
-#pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int chunk = ks * cpu + wig * CPW + cc;
-      const int off = chunk * 64 + c * 16;
-      va[cc] = ldg_stream(pa + off, pol);
-      vb[cc] = ldg_stream(pb + off, pol);
-      if constexpr (WT == W_NVFP4) {
-        const int kb = chunk * 8 + c * 2;
-        sa[cc] = ldg_u16_stream(a.bs + (size_t)ra * a.ldbs + kb, pol);
-        sb[cc] = ldg_u16_stream(a.bs + (size_t)rb * a.ldbs + kb, pol);
-      } else {
-        sa[cc] = 0;
-        sb[cc] = 0;
+  // Producer: weights by bulk copy (two 8-row blocks per full contiguous tile, else a
+  // copy per row), the unit's scales by cp.async; all complete on full[s].
+  auto issue = [&](int i) {
+    const uint64_t pol = policy_evict_first();
+    const int u = first + i * stride;
+    const int s = i % NS;
+    const int tg = u / ksplit, ks = u - tg * ksplit;
+    uint8_t* st = stages + (size_t)s * SG.bytes;
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(RT * 16 * UB));
+    __syncwarp();
+    for (int rt = 0; rt < RT; ++rt) {
+      const int t = tg * RT + rt;
+      if (contiguous && whole_tile(t)) {
+        if (lane < 2) {
+          bool ok;
+          const int row = row_of(t, lane * 8, ok);
+          bulk_g2s(st + rt * TILE + tile_row_offset(lane * 8, UB), a.w + (size_t)row * a.ldw,
+                   (uint32_t)(8 * UB), &full[s], pol);
+        }
+      } else if (lane < 16) {
+        bool ok;
+        const int row = row_of(t, lane, ok);
+        bulk_g2s(st + rt * TILE + tile_row_offset(lane, UB),
+                 a.w + (size_t)row * a.ldw + (size_t)ks * UB, (uint32_t)UB, &full[s], pol);
       }
-    }
-  };
-
-  // Running argmax key of this thread's token (threads with i == 0 of a token).
-  unsigned long long best = 0ull;
-  const bool do_argmax = a.am_keys != nullptr;
-
-  auto process = [&](int u, const uint4(&va)[CPW], const uint4(&vb)[CPW],
-                     const uint32_t(&sa)[CPW], const uint32_t(&sb)[CPW], int it) {
-    const int tile = u / ksplit, ks = u - tile * ksplit;
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
-#pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int chunk = ks * cpu + wig * CPW + cc;
-      uint4 xf[NT][Q];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int t = nt * 8 + g;
-#pragma unroll
-        for (int q = 0; q < Q; ++q) {
-          xf[nt][q] = (t < M) ? *reinterpret_cast<const uint4*>(
-                                    xs + (size_t)t * srow + ((chunk * Q + q) * 4 + c) * 16)
-                              : make_uint4(0u, 0u, 0u, 0u);
+      if (staged_scales(t)) {
+        // 16 raw scales: 16 * esz bytes = esz chunks of 16 B (SiLU: 8 gate + 8 up values)
+        const uint8_t* sbase = reinterpret_cast<const uint8_t*>(a.scale);
+        if (lane < esz) {
+          const int half_chunks = esz / 2;  // 16-B chunks per 8 values
+          const int h = lane / half_chunks, j = lane - h * half_chunks;
+          const size_t first_val = silu ? (size_t)(h ? N + t * 8 : t * 8) : (size_t)t * 16 + 8 * h;
+          cp_async16(st + SG.rsoff + rt * 64 + h * 8 * esz + j * 16, sbase + first_val * esz + j * 16);
         }
       }
-      chunk_mma<WT, NT>(acc, va[cc], vb[cc], sa[cc], sb[cc], xf);
-    }
-    // Cross-warp reduction of the group's partial tiles (double-buffered by `it`).
-    float* rbuf = red + (size_t)((grp * 2 + (it & 1)) * W) * 32 * NT * 4;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      *reinterpret_cast<float4*>(rbuf + ((size_t)(wig * 32 + lane) * NT + nt) * 4) =
-          make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    group_sync(1 + grp, gthreads);
-
-    // One thread per (token, tile row): gtid = tok * 16 + i (gthreads >= 16 * M).
-    const int tok = gtid >> 4, i = gtid & 15;
-    const bool live = tok < M;
-    float rowsum = 0.f;
-    if (live) {
-      const int nt = tok >> 3, col = tok & 7;
-      const int src = (i & 7) * 4 + (col >> 1);
-      const int reg = ((i >> 3) << 1) | (col & 1);
-      for (int w = 0; w < W; ++w) rowsum += rbuf[((size_t)(w * 32 + src) * NT + nt) * 4 + reg];
-    }
-    if (ksplit > 1) {
-      float* wsp = a.ws + ((size_t)tile * ksplit + ks) * 256;
-      if (live) st_cg_f32(wsp + i * 16 + tok, rowsum);
-      __threadfence();
-      group_sync(1 + grp, gthreads);
-      if (gtid == 0) {
-        const unsigned prev = atomicAdd(&a.ws_cnt[tile], 1u);
-        flags[grp] = (prev == (unsigned)(ksplit - 1));
+      if constexpr (WT == W_NVFP4) {
+        // e4m3 block scales of this unit's k range: nch_u * 8 bytes per row, 8 at a time
+        for (int idx = lane; idx < 16 * a.nch_u; idx += 32) {
+          const int r = idx / a.nch_u, j = idx - r * a.nch_u;
+          bool ok;
+          const int row = row_of(t, r, ok);
+          cp_async8(st + SG.bsoff + (rt * 16 + r) * SG.sbr + j * 8,
+                    a.bs + (size_t)row * a.ldbs + (size_t)ks * a.nch_u * 8 + j * 8);
+        }
       }
-      group_sync(1 + grp, gthreads);
-      if (!flags[grp]) return;
-      __threadfence();
-      rowsum = 0.f;
-      if (live) {
-        const float* base = a.ws + (size_t)tile * ksplit * 256 + i * 16 + tok;
-        for (int s = 0; s < ksplit; ++s) rowsum += ld_cg_f32(base + (size_t)s * 256);
-      }
-      if (gtid == 0) a.ws_cnt[tile] = 0u;  // every arrival for this tile has happened
     }
-
-    if (silu) {
-      // Rows 0..7 are gate, 8..15 up; lane i + 8 of the same token holds up's sum.
-      const float up = __shfl_down_sync(0xffffffffu, rowsum, 8);
-      const int n = tile * 8 + i;
-      if (live && i < 8 && n < N) {
-        const float us = unscale[tok];
-        const float gv = rowsum * us * load_row_scale(a.scale, a.scale_kind, n);
-        const float uv = up * us * load_row_scale(a.scale, a.scale_kind, (int64_t)N + n);
-        const __nv_bfloat16 o = __float2bfloat16_rn(silu_f32(gv) * uv);
-        reinterpret_cast<__nv_bfloat16*>(a.y)[(size_t)tok * a.ldy + n] = o;
-      }
-      return;
-    }
-
-    const int n = tile * 16 + i;
-    const bool valid = live && n < N;
-    uint32_t bits = 0;
-    if (valid) {
-      const float v = rowsum * unscale[tok] * load_row_scale(a.scale, a.scale_kind, n);
-      const __nv_bfloat16 o = __float2bfloat16_rn(v);
-      bits = (uint32_t)__bfloat16_as_ushort(o);
-      void* dst = a.y;
-      int64_t ld = a.ldy, col = n;
-      if (a.split_n > 0 && n >= a.split_n) {
-        dst = a.y2;
-        ld = a.ldy2;
-        col = n - a.split_n;
-      }
-      if (a.out_f32)
-        reinterpret_cast<float*>(dst)[(size_t)tok * ld + col] = __bfloat162float(o);
-      else
-        reinterpret_cast<__nv_bfloat16*>(dst)[(size_t)tok * ld + col] = o;
-    }
-    if (do_argmax) {
-      unsigned long long key = valid ? argmax_key(bits, (uint32_t)(a.row_offset + n)) : 0ull;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-        key = other > key ? other : key;
-      }
-      if (i == 0 && key > best) best = key;
-    }
+    cp_async_arrive(&full[s]);
   };
 
-  // Prologue: weight loads of the first S-1 units go out before waiting on the
-  // previous kernel (the weights do not depend on it).
-#pragma unroll
-  for (int s = 0; s < S - 1; ++s) {
-    const int u = first + s * stride;
-    if (u < n_units) load(u, ring.va[s], ring.vb[s], ring.sa[s], ring.sb[s]);
+  if (warp == 0) {
+    const int pre = my_units < NS ? my_units : NS;
+    for (int i = 0; i < pre; ++i) issue(i);
   }
+  // The weights and scales do not depend on the previous kernel; the activations may.
   pdl_wait();
   stage_rows<WT>(xs, unscale, M, K, [&](int r) {
     return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
   });
   __syncthreads();
 
-  int it = 0;
-  for (int base = first; base < n_units; base += S * stride) {
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    int issued = my_units < NS ? my_units : NS;
+    for (int i = NS; i < my_units; ++i) {
+      if (!mbar_wait(&empty[i % NS], ((i / NS) & 1) ^ 1)) {
+        record_error(a.err, ERR_WAIT_EMPTY);
+        break;
+      }
+      issue(i);
+      issued = i + 1;
+    }
+    // No copy may still be landing when the CTA exits.
+    for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+      if (!mbar_wait(&full[j % NS], (j / NS) & 1)) record_error(a.err, ERR_DRAIN);
+  } else if (warp > E) {
+    // ---------------------------------------------------------------- consumers
+    const int cw = warp - 1 - E;
+    const int rt = cw / KSL, kq = cw - rt * KSL;
+    const bool scale_lane = per_row && (kq == 0) && (c == 0);  // hands the row scales over
+    for (int i = 0; i < my_units; ++i) {
+      const int u = first + i * stride;
+      const int tg = u / ksplit, ks = u - tg * ksplit;
+      const int t = tg * RT + rt;
+      const int s = i % NS;
+      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+        record_error(a.err, ERR_WAIT_FULL);
+        break;
+      }
+      const uint8_t* st = stages + (size_t)s * SG.bytes;
+      float r0 = 0.f, r1 = 0.f;
+      if (scale_lane) {
+        if (staged_scales(t)) {
+          const uint8_t* rsb = st + SG.rsoff + rt * 64;
+          if (esz == 2) {
+            r0 = bf16_bits_to_f32(*reinterpret_cast<const unsigned short*>(rsb + pg * 2));
+            r1 = bf16_bits_to_f32(*reinterpret_cast<const unsigned short*>(rsb + pg8 * 2));
+          } else {
+            r0 = *reinterpret_cast<const float*>(rsb + pg * 4);
+            r1 = *reinterpret_cast<const float*>(rsb + pg8 * 4);
+          }
+        } else {  // ragged last tile or unaligned scales
+          bool oka, okb;
+          r0 = load_row_scale(a.scale, a.scale_kind, row_of(t, pg, oka));
+          r1 = load_row_scale(a.scale, a.scale_kind, row_of(t, pg8, okb));
+        }
+      }
+      const uint8_t* wt = st + (size_t)rt * TILE;
+      const uint8_t* rowa = wt + tile_row_offset(pg, UB) + c * 16;
+      const uint8_t* rowb = wt + tile_row_offset(pg8, UB) + c * 16;
+      const uint8_t* sca = st + SG.bsoff + (rt * 16 + pg) * SG.sbr + c * 2;
+      const uint8_t* scb = st + SG.bsoff + (rt * 16 + pg8) * SG.sbr + c * 2;
+      float acc[2][NT][4];
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int u = base + s * stride;
-      if (u >= n_units) break;
-      const int un = u + (S - 1) * stride;
-      const int nxt = (s + S - 1) % S;
-      if (un < n_units) load(un, ring.va[nxt], ring.vb[nxt], ring.sa[nxt], ring.sb[nxt]);
-      process(u, ring.va[s], ring.vb[s], ring.sa[s], ring.sb[s], it);
-      ++it;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[h][nt][r] = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int cl = kq * CPW + cc;
+        const int ch = ks * a.nch_u + cl;
+        const uint4 va = lds128(rowa + cl * 64);
+        const uint4 vb = lds128(rowb + cl * 64);
+        uint32_t sa = 0, sb = 0;
+        if constexpr (WT == W_NVFP4) {
+          sa = *reinterpret_cast<const unsigned short*>(sca + cl * 8);
+          sb = *reinterpret_cast<const unsigned short*>(scb + cl * 8);
+        }
+        uint4 xf[NT][Q];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int tk = nt * 8 + g;
+#pragma unroll
+          for (int q = 0; q < Q; ++q)
+            xf[nt][q] = (tk < M) ? lds128(xs + (size_t)tk * srow + ((ch * Q + q) * 4 + c) * 16)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+        }
+        chunk_mma<WT, NT>(acc[cc & 1], va, vb, sa, sb, xf);
+      }
+      __syncwarp();  // every lane's reads of the stage are complete
+      if (lane == 0) mbar_arrive(&empty[s]);
+      const int rs = i % RS;
+      if (!mbar_wait(&rfree[rs], ((i / RS) & 1) ^ 1)) {
+        record_error(a.err, ERR_WAIT_RFREE);
+        break;
+      }
+      float* dst = red + ((size_t)(rs * W + cw) * 32 + lane) * NT * 4;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float4*>(dst + nt * 4) =
+            make_float4(acc[0][nt][0] + acc[1][nt][0], acc[0][nt][1] + acc[1][nt][1],
+                        acc[0][nt][2] + acc[1][nt][2], acc[0][nt][3] + acc[1][nt][3]);
+      if (scale_lane) {
+        sred[rs * 64 + rt * 16 + pg] = r0;
+        sred[rs * 64 + rt * 16 + pg8] = r1;
+      }
+      __syncwarp();  // orders the lanes' stores before the release
+      if (lane == 0) mbar_arrive(&rfull[rs]);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue warps
+    // Epilogue warp e takes units i = e, e + E, ...  Lane L owns the outputs of MMA
+    // lane L: physical rows (pg, pg8) x tokens (nt*8 + 2c + {0,1}) of every row tile.
+    const int e = warp - 1;
+    const float scalar_scale = per_row ? 0.f : load_row_scale(a.scale, a.scale_kind, 0);
+    unsigned long long best[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) best[nt][0] = best[nt][1] = 0ull;
+    const bool do_argmax = a.am_keys != nullptr;
+    for (int i = e; i < my_units; i += E) {
+      const int u = first + i * stride;
+      const int tg = u / ksplit, ks = u - tg * ksplit;
+      const int rs = e;
+      if (!mbar_wait(&rfull[rs], (i / RS) & 1)) {
+        record_error(a.err, ERR_WAIT_RED);
+        break;
+      }
+      float v[kMaxRT][NT][4];
+      float scl[kMaxRT][2];
+#pragma unroll
+      for (int rt = 0; rt < kMaxRT; ++rt) {
+        if (rt >= RT) break;
+        scl[rt][0] = per_row ? sred[rs * 64 + rt * 16 + pg] : scalar_scale;
+        scl[rt][1] = per_row ? sred[rs * 64 + rt * 16 + pg8] : scalar_scale;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+          int kq = 0;
+          for (; kq + 1 < KSL; kq += 2) {  // two chains; fixed order
+            const float4 p = *reinterpret_cast<const float4*>(
+                red + ((size_t)(rs * W + rt * KSL + kq) * 32 + lane) * NT * 4 + nt * 4);
+            const float4 q = *reinterpret_cast<const float4*>(
+                red + ((size_t)(rs * W + rt * KSL + kq + 1) * 32 + lane) * NT * 4 + nt * 4);
+            s0.x += p.x; s0.y += p.y; s0.z += p.z; s0.w += p.w;
+            s1.x += q.x; s1.y += q.y; s1.z += q.z; s1.w += q.w;
+          }
+          if (kq < KSL) {
+            const float4 p = *reinterpret_cast<const float4*>(
+                red + ((size_t)(rs * W + rt * KSL + kq) * 32 + lane) * NT * 4 + nt * 4);
+            s0.x += p.x; s0.y += p.y; s0.z += p.z; s0.w += p.w;
+          }
+          v[rt][nt][0] = s0.x + s1.x;
+          v[rt][nt][1] = s0.y + s1.y;
+          v[rt][nt][2] = s0.z + s1.z;
+          v[rt][nt][3] = s0.w + s1.w;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfree[rs]);
+
+      bool finish = true;
+      if (ksplit > 1) {
+        // Split-K fix-up: publish this split's tile sums; the last split sums all of
+        // them in split order and resets the counter.
+        float* wsp = a.ws + ((size_t)tg * ksplit + ks) * RT * 256;
+#pragma unroll
+        for (int rt = 0; rt < kMaxRT; ++rt) {
+          if (rt >= RT) break;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) st_cg_f32(wsp + rt * 256 + (nt * 4 + r) * 32 + lane, v[rt][nt][r]);
+        }
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(&a.ws_cnt[tg], 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        finish = prev == (unsigned)(ksplit - 1);
+        if (finish) {
+          __threadfence();
+#pragma unroll
+          for (int rt = 0; rt < kMaxRT; ++rt) {
+            if (rt >= RT) break;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                float acc = 0.f;
+                const float* base = a.ws + (size_t)tg * ksplit * RT * 256 + rt * 256 + (nt * 4 + r) * 32 + lane;
+                for (int k2 = 0; k2 < ksplit; ++k2) acc += ld_cg_f32(base + (size_t)k2 * RT * 256);
+                v[rt][nt][r] = acc;
+              }
+          }
+          if (lane == 0) a.ws_cnt[tg] = 0u;
+        }
+      }
+
+      if (finish) {
+#pragma unroll
+        for (int rt = 0; rt < kMaxRT; ++rt) {
+          if (rt >= RT) break;
+          const int t = tg * RT + rt;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              const int tok = nt * 8 + 2 * c + p;
+              const bool tok_ok = tok < M;
+              const float us = tok_ok ? unscale[tok] : 0.f;
+              if (silu) {
+                // physical rows < 8 are gate, >= 8 up; both hold column t*8 + g
+                const int n = t * 8 + g;
+                if (tok_ok && n < N) {
+                  const bool odd = g & 1;  // MMA row g is the up row for odd g
+                  const float gsum = odd ? v[rt][nt][2 + p] : v[rt][nt][p];
+                  const float usum = odd ? v[rt][nt][p] : v[rt][nt][2 + p];
+                  const float gsc = odd ? scl[rt][1] : scl[rt][0];
+                  const float usc = odd ? scl[rt][0] : scl[rt][1];
+                  reinterpret_cast<__nv_bfloat16*>(a.y)[(size_t)tok * a.ldy + n] =
+                      __float2bfloat16_rn(silu_f32(gsum * us * gsc) * (usum * us * usc));
+                }
+                continue;
+              }
+              unsigned long long key = 0ull;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int n = t * 16 + (h ? pg8 : pg);
+                if (!(tok_ok && n < N)) continue;
+                const __nv_bfloat16 o = __float2bfloat16_rn(v[rt][nt][2 * h + p] * us * scl[rt][h]);
+                void* dst = a.y;
+                int64_t ld = a.ldy, col = n;
+                if (a.split_n > 0 && n >= a.split_n) {
+                  dst = a.y2;
+                  ld = a.ldy2;
+                  col = n - a.split_n;
+                }
+                if (a.out_f32)
+                  reinterpret_cast<float*>(dst)[(size_t)tok * ld + col] = __bfloat162float(o);
+                else
+                  reinterpret_cast<__nv_bfloat16*>(dst)[(size_t)tok * ld + col] = o;
+                const unsigned long long k =
+                    argmax_key((uint32_t)__bfloat16_as_ushort(o), (uint32_t)(a.row_offset + n));
+                key = k > key ? k : key;
+              }
+              if (do_argmax) {
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                  const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                  key = other > key ? other : key;
+                }
+                if (key > best[nt][p]) best[nt][p] = key;
+              }
+            }
+          }
+        }
+      }
+    }
+
+    if (do_argmax) {
+      if (g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const int tok = nt * 8 + 2 * c + p;
+            if (tok < M && best[nt][p] != 0ull) atomicMax(&a.am_keys[tok], best[nt][p]);
+          }
+      }
+      __threadfence();
+      __syncwarp();
+      unsigned prev = 0;
+      if (lane == 0) prev = atomicAdd(a.am_count, 1u);
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      if (prev == gridDim.x * (unsigned)E - 1) {
+        __threadfence();
+        if (lane < M) {
+          const unsigned long long key = atomicExch(&a.am_keys[lane], 0ull);
+          if (a.am_out) a.am_out[lane] = (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+          if (a.am_key_out) a.am_key_out[lane] = key;
+        }
+        if (lane == 0) *a.am_count = 0u;
+      }
     }
   }
   pdl_trigger();
-
-  if (do_argmax) {
-    const int tok = gtid >> 4, i = gtid & 15;
-    if (i == 0 && tok < M && best != 0ull) atomicMax(&a.am_keys[tok], best);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const unsigned prev = atomicAdd(a.am_count, 1u);
-      flags[0] = (prev == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (flags[0]) {
-      __threadfence();
-      if (tid < M) {
-        const unsigned long long key = atomicExch(&a.am_keys[tid], 0ull);
-        if (a.am_out) a.am_out[tid] = (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
-        if (a.am_key_out) a.am_key_out[tid] = key;
-      }
-      if (tid == 0) *a.am_count = 0u;
-    }
-  }
 }
 
 // Decode argmax keys (after a cross-rank MAX reduction of the keys) into row ids.
@@ -266,9 +455,10 @@ using DenseKernel = void (*)(const DenseArgs);
 template <int WT, int NT>
 DenseKernel pick_cpw(int cpw) {
   switch (cpw) {
-    case 1: return dense_gemv_kernel<WT, NT, 1, 4>;
-    case 2: return dense_gemv_kernel<WT, NT, 2, 3>;
-    case 4: return dense_gemv_kernel<WT, NT, 4, 2>;
+    case 1: return dense_gemv_kernel<WT, NT, 1>;
+    case 2: return dense_gemv_kernel<WT, NT, 2>;
+    case 4: return dense_gemv_kernel<WT, NT, 4>;
+    case 8: return dense_gemv_kernel<WT, NT, 8>;
     default: return nullptr;
   }
 }
@@ -301,7 +491,7 @@ int launch_dense(const DenseArgs& a, int wtype, int nt, int cpw, int grid, size_
   DenseKernel k = dense_kernel(wtype, nt, cpw);
   if (!k) return 1;
   if (!prepare_kernel((const void*)k)) return 2;
-  return launch_with_pdl((const void*)k, a, grid, a.W * a.G * 32, smem, a.pdl, stream);
+  return launch_with_pdl((const void*)k, a, grid, (a.W + 1 + a.E) * 32, smem, a.pdl, stream);
 }
 
 }  // namespace fnx

@@ -78,75 +78,122 @@ int chunk_k(int wt) {
   }
 }
 
-size_t dense_smem(int M, int K, int W, int G, int NT) {
-  return (size_t)M * fnx::stage_row_bytes(K) + 64 + (size_t)G * 2 * W * 32 * NT * 16 + 64;
-}
-
 constexpr size_t kMaxSmem = 227 * 1024;
 
-// Planner for the dense GEMVs.  One 16-row tile (8 SiLU outputs) per unit; the warps of
-// a group split the tile's k range; k is also split across groups (ksplit) when the tile
-// count alone cannot keep every SM streaming.
-int plan_dense(int M, int N, int K, int wt, int silu, fnx_gemv_cfg* out) {
+// Geometry of one dense call.  A work unit is RT 16-row tiles x (K / ksplit); each of
+// the W consumer warps streams CPW 64-byte chunks of every row of one tile; the weight
+// ring has NS stages of RT tiles of TILE bytes (two 8-row halves, see tile_half_offset).
+struct DensePlan {
+  int ksplit, W, RT, CPW, NS, E, UB, TILE, nch_u, row_tiles, tile_groups, n_units, wt;
+  size_t smem;
+};
+
+int finish_plan(int M, int K, int NT, DensePlan& p) {
+  p.E = 2;
+  p.UB = p.nch_u * 64;
+  p.TILE = fnx::tile_bytes(p.UB);
+  p.tile_groups = (p.row_tiles + p.RT - 1) / p.RT;
+  p.n_units = p.tile_groups * p.ksplit;
+  const int stage = fnx::dense_stage(p.wt == FNX_W_NVFP4, p.RT, p.TILE, p.nch_u).bytes;
+  const fnx::DenseLayout L0 = fnx::dense_layout(M, K, p.W, 0, p.E, NT, stage);
+  if ((size_t)L0.total + 2 * (size_t)stage + 256 > kMaxSmem)
+    return fail(FNX_EUNSUPPORTED, "shared memory: M=%d K=%d leaves no room for 2 stages", M, K);
+  const int ns = (int)((kMaxSmem - L0.total - 256) / stage);
+  p.NS = std::max(2, std::min(ns, 8));
+  p.smem = fnx::dense_layout(M, K, p.W, p.NS, p.E, NT, stage).total;
+  return FNX_OK;
+}
+
+// Consumer warps W (any count up to 16), chunks per warp CPW and row tiles per unit RT
+// for a unit of `nch_u` 64-byte chunks per row: prefer 8..16 warps, each streaming one
+// to eight chunks; a short unit takes several row tiles so 8 warps still have work.
+bool tile_unit(int nch_u, int& W, int& CPW, int& RT) {
+  for (int lo : {8, 4}) {
+    for (int cpw : {1, 2, 4, 8}) {
+      if (nch_u % cpw) continue;
+      const int w = nch_u / cpw;
+      if (w >= lo && w <= 16) {
+        W = w;
+        CPW = cpw;
+        RT = 1;
+        return true;
+      }
+    }
+  }
+  if (nch_u < 8 && 8 % nch_u == 0) {
+    RT = std::min(4, 8 / nch_u);
+    W = RT * nch_u;
+    CPW = 1;
+    return true;
+  }
+  for (int cpw : {1, 2, 4, 8}) {
+    if (nch_u % cpw == 0 && nch_u / cpw <= 16) {
+      W = nch_u / cpw;
+      CPW = cpw;
+      RT = 1;
+      return true;
+    }
+  }
+  return false;
+}
+
+// k2 (down projection) tiling: the most 16-row tiles per unit (up to 4) whose
+// RT x (I / 128 / CPW) consumer warps fit in 16 and whose rows divide H.
+bool down_tiling(int H, int I, int& CPW, int& RT) {
+  const int ch2 = I / 128;
+  for (int rt = 4; rt >= 1; --rt) {
+    if (H % (16 * rt)) continue;
+    for (int c : {1, 2, 4})
+      if (ch2 % c == 0 && rt * (ch2 / c) <= 16) {
+        CPW = c;
+        RT = rt;
+        return true;
+      }
+  }
+  return false;
+}
+
+int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, DensePlan& p) {
   const int CH = chunk_k(wt);
   if (K <= 0 || K % CH)
     return fail(FNX_EUNSUPPORTED, "K=%d must be a positive multiple of %d for this weight type",
                 K, CH);
   const int nch = K / CH;
-  const int row_tiles = silu ? (N + 7) / 8 : (N + 15) / 16;
-  const int sms = fnx::num_sms();
-  const int min_w = std::max(1, (M + 1) / 2);  // one output thread per (token, tile row)
-  int best_ks = -1, best_w = 0, best_cpw = 0;
-  for (int ks = 1; ks <= nch; ++ks) {
-    if (nch % ks) continue;
-    const int cpu = nch / ks;
-    int w = 0, cpw = 0;
-    for (int c : {2, 1, 4}) {
-      if (cpu % c) continue;
-      const int ww = cpu / c;
-      if (ww >= min_w && ww <= 16) {
-        w = ww;
-        cpw = c;
-        break;
-      }
-    }
-    if (!w) continue;
-    if (best_ks < 0) {
-      best_ks = ks;
-      best_w = w;
-      best_cpw = cpw;
-    }
-    if ((int64_t)row_tiles * best_ks >= 3 * sms) break;
-    if (ks > best_ks) {
-      best_ks = ks;
-      best_w = w;
-      best_cpw = cpw;
-    }
+  const int NT = M > 8 ? 2 : 1;
+  p.wt = wt;
+  p.row_tiles = silu ? (N + 7) / 8 : (N + 15) / 16;
+  if (req) {
+    p.ksplit = req->ksplit;
+    p.W = req->warps;
+    p.CPW = req->chunks_per_warp;
+    p.RT = std::max(1, req->groups);
+    if (p.ksplit < 1 || nch % p.ksplit)
+      return fail(FNX_EINVAL, "ksplit=%d must divide K/%d = %d", p.ksplit, CH, nch);
+    p.nch_u = nch / p.ksplit;
+    if (p.W < 1 || p.W > 16 || p.RT > 4 || p.W % p.RT ||
+        (p.CPW != 1 && p.CPW != 2 && p.CPW != 4 && p.CPW != 8) || (p.W / p.RT) * p.CPW != p.nch_u)
+      return fail(FNX_EINVAL,
+                  "need warps <= 16, row tiles <= 4 dividing warps, chunks_per_warp in {1,2,4,8} "
+                  "and (warps / row_tiles) * chunks_per_warp == %d chunks per unit", p.nch_u);
+    return finish_plan(M, K, NT, p);
   }
-  if (best_ks < 0)
-    return fail(FNX_EUNSUPPORTED, "no tiling of K=%d (%d chunks) for M=%d", K, nch, M);
-  out->ksplit = best_ks;
-  out->warps = best_w;
-  out->chunks_per_warp = best_cpw;
-  // groups share a CTA through named barriers 1..groups (ids 0..15 exist; keep <= 8)
-  out->groups = std::max(1, std::min(std::min(16 / best_w, 8), row_tiles * best_ks));
-  out->grid = 0;
-  return FNX_OK;
-}
-
-int check_cfg(int M, int K, int wt, const fnx_gemv_cfg& c) {
-  const int CH = chunk_k(wt);
-  if (K % CH) return fail(FNX_EUNSUPPORTED, "K=%d not a multiple of %d", K, CH);
-  const int nch = K / CH;
-  if (c.chunks_per_warp != 1 && c.chunks_per_warp != 2 && c.chunks_per_warp != 4)
-    return fail(FNX_EINVAL, "chunks_per_warp must be 1, 2 or 4");
-  if (c.warps < 1 || c.groups < 1 || c.groups > 8 || c.warps * c.groups > 16)
-    return fail(FNX_EINVAL, "need 1 <= groups <= 8 and warps * groups <= 16");
-  if (c.warps * 32 < 16 * M)
-    return fail(FNX_EINVAL, "warps=%d too few for M=%d (need warps >= M/2)", c.warps, M);
-  if (c.ksplit < 1 || (int64_t)c.warps * c.chunks_per_warp * c.ksplit != nch)
-    return fail(FNX_EINVAL, "warps * chunks_per_warp * ksplit must equal K/%d = %d", CH, nch);
-  return FNX_OK;
+  const int sms = fnx::num_sms();
+  // Smallest k split whose unit tiles onto the consumer warps and that gives every SM
+  // two units; without such a split, the largest split that tiles.
+  int best = -1;
+  for (int k = 1; k <= nch; ++k) {
+    if (nch % k) continue;
+    int w, cpw, rt;
+    if (!tile_unit(nch / k, w, cpw, rt)) continue;
+    best = k;
+    if ((int64_t)p.row_tiles * k >= sms) break;
+    if (nch / k <= 4) break;  // keep at least 4 chunks (256 B of each row) per unit
+  }
+  if (best < 0) return fail(FNX_EUNSUPPORTED, "no tiling of K=%d (%d chunks)", K, nch);
+  p.ksplit = best;
+  p.nch_u = nch / best;
+  tile_unit(p.nch_u, p.W, p.CPW, p.RT);
+  return finish_plan(M, K, NT, p);
 }
 
 struct DenseCall {
@@ -189,8 +236,8 @@ int run_dense(const DenseCall& c) {
     return fail(FNX_EINVAL, "weight rows must be 16-byte aligned, ldw=%lld < %lld bytes or not a "
                 "multiple of 16", (long long)c.ldw, (long long)row_bytes);
   if (c.wt == FNX_W_NVFP4) {
-    if (!c.bs || c.ldbs < c.K / 16 || c.ldbs % 2 || !aligned(c.bs, 2))
-      return fail(FNX_EINVAL, "block scales must be [N, K/16] with an even row stride");
+    if (!c.bs || c.ldbs < c.K / 16 || c.ldbs % 8 || !aligned(c.bs, 8))
+      return fail(FNX_EINVAL, "block scales must be [N, K/16], 8-byte aligned rows");
   }
   if (c.scale_kind < FNX_SCALE_NONE || c.scale_kind > FNX_SCALE_BF16_ROW)
     return fail(FNX_EINVAL, "bad scale kind %d", c.scale_kind);
@@ -208,42 +255,29 @@ int run_dense(const DenseCall& c) {
   if (c.row_offset < 0 || c.row_offset + c.N > 0xFFFFFFFFLL)
     return fail(FNX_EINVAL, "row ids must fit in 32 bits");
 
-  fnx_gemv_cfg cfg;
-  if (c.cfg) {
-    cfg = *c.cfg;
-  } else {
-    const int rc = plan_dense(c.M, c.N, c.K, c.wt, c.silu, &cfg);
-    if (rc) return rc;
-  }
-  int rc = check_cfg(c.M, c.K, c.wt, cfg);
+  DensePlan p;
+  int rc = plan_dense(c.M, c.N, c.K, c.wt, c.silu, c.cfg, p);
   if (rc) return rc;
-
   const int NT = c.M > 8 ? 2 : 1;
-  const int row_tiles = c.silu ? (c.N + 7) / 8 : (c.N + 15) / 16;
-  const int64_t n_units = (int64_t)row_tiles * cfg.ksplit;
-  if (n_units > 0x7FFFFFFF) return fail(FNX_EUNSUPPORTED, "too many tiles");
-  const size_t smem = dense_smem(c.M, c.K, cfg.warps, cfg.groups, NT);
-  if (smem > kMaxSmem)
-    return fail(FNX_EUNSUPPORTED, "shared memory %zu > %zu (M=%d K=%d)", smem, kMaxSmem, c.M, c.K);
 
   const bool want_argmax = c.argmax_out || c.argmax_key_out;
-  if (cfg.ksplit > 1) {
+  if (p.ksplit > 1) {
+    const int64_t need = (int64_t)p.tile_groups * p.ksplit * p.RT * 256;
     if (!c.ws || !c.ws->partials || !c.ws->counters)
-      return fail(FNX_EINVAL, "ksplit=%d needs a workspace", cfg.ksplit);
-    if (c.ws->partial_floats < n_units * 256 || c.ws->n_counters < row_tiles)
+      return fail(FNX_EINVAL, "ksplit=%d needs a workspace", p.ksplit);
+    if (c.ws->partial_floats < need || c.ws->n_counters < p.tile_groups)
       return fail(FNX_EINVAL, "workspace too small: need %lld floats and %d counters",
-                  (long long)(n_units * 256), row_tiles);
+                  (long long)need, p.tile_groups);
   }
   if (want_argmax && (!c.ws || !c.ws->argmax_keys || !c.ws->argmax_count))
     return fail(FNX_EINVAL, "argmax needs the workspace's argmax_keys/argmax_count");
 
-  const int threads = cfg.warps * cfg.groups * 32;
-  int grid = cfg.grid;
+  const int threads = (p.W + 1 + p.E) * 32;
+  int grid = c.cfg && c.cfg->grid > 0 ? c.cfg->grid : 0;
   if (grid <= 0) {
-    const int occ = fnx::dense_occupancy(c.wt, NT, cfg.chunks_per_warp, threads, smem);
-    if (occ <= 0) return fail(FNX_EUNSUPPORTED, "kernel does not fit on an SM (smem %zu)", smem);
-    const int64_t want = (n_units + cfg.groups - 1) / cfg.groups;
-    grid = (int)std::min<int64_t>(want, (int64_t)fnx::num_sms() * occ);
+    const int occ = fnx::dense_occupancy(c.wt, NT, p.CPW, threads, p.smem);
+    if (occ <= 0) return fail(FNX_EUNSUPPORTED, "kernel does not fit on an SM (smem %zu)", p.smem);
+    grid = (int)std::min<int64_t>(p.n_units, (int64_t)fnx::num_sms() * occ);
   }
 
   fnx::DenseArgs a = {};
@@ -268,23 +302,63 @@ int run_dense(const DenseCall& c) {
   a.row_offset = c.row_offset;
   a.ws = c.ws ? c.ws->partials : nullptr;
   a.ws_cnt = c.ws ? c.ws->counters : nullptr;
+  a.err = c.ws ? c.ws->error_flag : nullptr;
   a.M = c.M;
   a.N = c.N;
   a.K = c.K;
-  a.ksplit = cfg.ksplit;
+  a.ksplit = p.ksplit;
   a.silu = c.silu;
-  a.W = cfg.warps;
-  a.G = cfg.groups;
-  a.row_tiles = row_tiles;
-  a.n_units = (int)n_units;
+  a.W = p.W;
+  a.RT = p.RT;
+  a.NS = p.NS;
+  a.RS = p.E;
+  a.UB = p.UB;
+  a.TILE = p.TILE;
+  a.E = p.E;
+  a.nch_u = p.nch_u;
+  a.row_tiles = p.row_tiles;
+  a.tile_groups = p.tile_groups;
+  a.n_units = p.n_units;
   a.pdl = c.pdl;
-  rc = fnx::launch_dense(a, c.wt, NT, cfg.chunks_per_warp, grid, smem, c.stream);
+  rc = fnx::launch_dense(a, c.wt, NT, p.CPW, grid, p.smem, c.stream);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no kernel instance for this configuration");
   if (rc) return cuda_fail("dense GEMV launch");
   return FNX_OK;
 }
 
 }  // namespace
+
+// Launch geometry of the two MoE kernels for M tokens x R routes over E experts.
+struct MoeGeo {
+  int NT, w1, cpw1, ns1, w2, cpw2, rt2, ns2;
+  size_t smem1, smem2;
+};
+
+int moe_geometry(int M, int R, int E, int H, int I, MoeGeo& g) {
+  if (H % 128 || I % 128 || H <= 0 || I <= 0)
+    return fail(FNX_EUNSUPPORTED, "H=%d and I=%d must be multiples of 128", H, I);
+  g.NT = M > 8 ? 2 : 1;
+  // k1: consumers split H (chunks of 128) into W slices of CPW chunks.
+  int rt1 = 0;
+  if (!tile_unit(H / 128, g.w1, g.cpw1, rt1) || rt1 != 1 || g.cpw1 > 4)
+    return fail(FNX_EUNSUPPORTED, "H=%d: no gate/up tiling", H);
+  // k2: units of RT 16-row tiles; consumers = RT tiles x (I / 128 / CPW) k slices.
+  if (!down_tiling(H, I, g.cpw2, g.rt2)) return fail(FNX_EUNSUPPORTED, "I=%d: no down tiling", I);
+  g.w2 = g.rt2 * (I / 128 / g.cpw2);
+  const int RS = 2;
+  auto stages_for = [&](int kernel, int W, int RT) {
+    const fnx::MoeLayout L0 = fnx::moe_layout(kernel, M, R, E, H, I, W, 0, RS, g.NT, RT);
+    const int64_t ns = ((int64_t)kMaxSmem - L0.total - 256) / L0.stage_bytes;
+    return (int)std::min<int64_t>(ns, 8);
+  };
+  g.ns1 = stages_for(1, g.w1, 1);
+  g.ns2 = stages_for(2, g.w2, g.rt2);
+  if (g.ns1 < 2 || g.ns2 < 2)
+    return fail(FNX_EUNSUPPORTED, "MoE shared memory too small for M=%d, H=%d, I=%d", M, H, I);
+  g.smem1 = fnx::moe_layout(1, M, R, E, H, I, g.w1, g.ns1, RS, g.NT, 1).total;
+  g.smem2 = fnx::moe_layout(2, M, R, E, H, I, g.w2, g.ns2, RS, g.NT, g.rt2).total;
+  return FNX_OK;
+}
 
 extern "C" {
 
@@ -295,22 +369,27 @@ int fnx_plan_gemv(int M, int N, int K, int w_dtype, int fused_silu, int argmax,
   if (!out) return fail(FNX_EINVAL, "null out");
   if (M < 1 || M > FNX_MAX_M) return fail(FNX_EINVAL, "M=%d must be in [1, 16]", M);
   if (w_dtype < FNX_W_INT8 || w_dtype > FNX_W_NVFP4) return fail(FNX_EINVAL, "bad w_dtype");
-  return plan_dense(M, N, K, w_dtype, fused_silu, out);
+  DensePlan p;
+  const int rc = plan_dense(M, N, K, w_dtype, fused_silu, nullptr, p);
+  if (rc) return rc;
+  out->warps = p.W;
+  out->chunks_per_warp = p.CPW;
+  out->groups = p.RT;
+  out->ksplit = p.ksplit;
+  out->grid = 0;
+  return FNX_OK;
 }
 
 int fnx_gemv_workspace_need(int M, int N, int K, int w_dtype, int fused_silu,
                             const fnx_gemv_cfg* cfg, int64_t* partial_floats,
                             int64_t* n_counters) {
-  fnx_gemv_cfg c;
-  if (cfg) {
-    c = *cfg;
-  } else {
-    const int rc = fnx_plan_gemv(M, N, K, w_dtype, fused_silu, 0, &c);
-    if (rc) return rc;
-  }
-  const int64_t row_tiles = fused_silu ? (N + 7) / 8 : (N + 15) / 16;
-  if (partial_floats) *partial_floats = c.ksplit > 1 ? row_tiles * c.ksplit * 256 : 0;
-  if (n_counters) *n_counters = c.ksplit > 1 ? row_tiles : 0;
+  g_err.clear();
+  DensePlan p;
+  const int rc = plan_dense(M, N, K, w_dtype, fused_silu, cfg, p);
+  if (rc) return rc;
+  if (partial_floats)
+    *partial_floats = p.ksplit > 1 ? (int64_t)p.tile_groups * p.ksplit * p.RT * 256 : 0;
+  if (n_counters) *n_counters = p.ksplit > 1 ? p.tile_groups : 0;
   return FNX_OK;
 }
 
@@ -358,14 +437,21 @@ int fnx_w4a16_nvfp4_gemv(const void* x, int64_t ldx, const void* wq, int64_t ldw
   return run_dense(c);
 }
 
-int fnx_moe_workspace_bytes(int M, int R, int H, int I, int64_t* act_bytes,
-                            int64_t* partial_bytes, int64_t* counter_bytes) {
+int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, int I,
+                            fnx_moe_workspace_sizes* out) {
   g_err.clear();
-  if (M < 1 || R < 1 || H < 16 || I < 1) return fail(FNX_EINVAL, "bad MoE shape");
-  const int64_t pairs = (int64_t)M * (R + 1);
-  if (act_bytes) *act_bytes = pairs * I * 2;
-  if (partial_bytes) *partial_bytes = pairs * H * 4;
-  if (counter_bytes) *counter_bytes = (int64_t)(H / 16) * 4;
+  if (!out || max_m < 1 || max_routes < 1 || num_experts < 1 || H < 64 || I < 1)
+    return fail(FNX_EINVAL, "bad MoE shape");
+  MoeGeo geo;
+  if (int rc = moe_geometry(max_m, max_routes, num_experts, H, I, geo)) return rc;
+  const int64_t pairs = (int64_t)max_m * (max_routes + 1);
+  const int64_t dcap = std::min<int64_t>(num_experts, (int64_t)max_m * max_routes) + 1;
+  out->act = pairs * I * 2;
+  out->act_f16 = dcap * 16 * (2LL * I + 64);
+  out->pair_unscale = dcap * 16 * 4;
+  out->expert_counters = dcap * 4;
+  out->partials = pairs * H * 4;
+  out->counters = (int64_t)(H / 16) * 4;  // one per k2 row group (16 * RT rows, RT >= 1)
   return FNX_OK;
 }
 
@@ -381,8 +467,6 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   if (!topk_ids || !topk_weights) return fail(FNX_EINVAL, "null topk_ids / topk_weights");
   const int H = experts->hidden, I = experts->inter, E = experts->num_experts;
   if (E < 1 || E > 4096) return fail(FNX_EINVAL, "num_experts=%d must be in [1, 4096]", E);
-  if (H % 128 || I % 128 || H <= 0 || I <= 0)
-    return fail(FNX_EUNSUPPORTED, "H=%d and I=%d must be multiples of 128", H, I);
   if (!experts->w13 || !experts->w13_scale || !experts->w13_gscale || !experts->w2 ||
       !experts->w2_scale || !experts->w2_gscale)
     return fail(FNX_EINVAL, "null expert tensor");
@@ -401,43 +485,17 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
     if (!aligned(shared->w13, 16) || !aligned(shared->w2, 16))
       return fail(FNX_EINVAL, "shared expert weights must be 16-byte aligned");
   }
-  if (!ws->act || !ws->partials || !ws->counters || ws->max_m < M || ws->max_routes < R)
+  if (!ws->act || !ws->act_f16 || !ws->pair_unscale || !ws->expert_counters || !ws->partials ||
+      !ws->counters || ws->max_m < M || ws->max_routes < R)
     return fail(FNX_EINVAL, "MoE workspace missing or sized for fewer tokens/routes");
-
+  if (!aligned(ws->act_f16, 16) || !aligned(ws->act, 16))
+    return fail(FNX_EINVAL, "MoE workspace act buffers must be 16-byte aligned");
+  // The routes of one token address act rows t * (R + 1) + r of the workspace's
+  // (max_routes + 1)-wide layout only when R == max_routes; use the call's R instead.
   const int NT = M > 8 ? 2 : 1;
   const int sms = fnx::num_sms();
   const int has_shared = shared ? 1 : 0;
   const int dmax = std::min(E, M * R) + has_shared;
-
-  // k1: the warps of a group split H into 128-wide chunks.
-  const int ch1 = H / 128;
-  int w1 = ch1, cpw1 = 1;
-  if (w1 > 16 || w1 < 8) {
-    if (ch1 % 2 == 0 && ch1 / 2 >= 8 && ch1 / 2 <= 16) {
-      w1 = ch1 / 2;
-      cpw1 = 2;
-    } else {
-      return fail(FNX_EUNSUPPORTED, "H=%d: no k1 tiling (needs 8..32 chunks of 128)", H);
-    }
-  }
-  const int g1 = 1;
-  // k2: I in 128-wide chunks, several tiles per CTA.
-  const int ch2 = I / 128;
-  int w2 = ch2, cpw2 = 1;
-  if (w2 > 16) {
-    if (ch2 % 2 == 0 && ch2 / 2 <= 16) {
-      w2 = ch2 / 2;
-      cpw2 = 2;
-    } else {
-      return fail(FNX_EUNSUPPORTED, "I=%d: no k2 tiling", I);
-    }
-  }
-  const int g2 = std::max(1, std::min(16 / w2, 8));
-  const size_t smem1 = fnx::moe_up_smem(M, R, E, H, w1, g1, NT);
-  const size_t smem2 = fnx::moe_down_smem(M, R, E, I, w2, g2, NT);
-  if (smem1 > kMaxSmem || smem2 > kMaxSmem)
-    return fail(FNX_EUNSUPPORTED, "MoE shared memory %zu / %zu exceeds %zu", smem1, smem2,
-                kMaxSmem);
 
   fnx::MoeArgs a = {};
   a.x = x;
@@ -469,31 +527,47 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   a.swizzled = experts->scales_swizzled;
   a.e_lo = experts->expert_offset;
   a.act = ws->act;
+  a.act_f16 = static_cast<uint8_t*>(ws->act_f16);
+  a.pair_unscale = ws->pair_unscale;
+  a.ecnt = ws->expert_counters;
   a.part = ws->partials;
   a.cnt = ws->counters;
+  a.err = ws->error_flag;
   a.out = out;
   a.ldo = ldo;
   a.out_f32 = out_f32;
-  a.pdl = pdl;
+  a.RS = 2;
+  a.NT = NT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
+  MoeGeo geo;
+  if (int rc = moe_geometry(M, R, E, H, I, geo)) return rc;
+  const int w1 = geo.w1, cpw1 = geo.cpw1, ns1 = geo.ns1;
+  const int w2 = geo.w2, cpw2 = geo.cpw2, rt2 = geo.rt2, ns2 = geo.ns2;
+
   a.W = w1;
-  a.G = g1;
-  const int occ1 = fnx::moe_up_occupancy(NT, cpw1, w1 * g1 * 32, smem1);
+  a.CPW = cpw1;
+  a.NS = ns1;
+  a.pdl = pdl;
+  const size_t smem1 = geo.smem1;
+  const int occ1 = fnx::moe_up_occupancy(NT, cpw1, (w1 + 2) * 32, smem1);
   if (occ1 <= 0) return fail(FNX_EUNSUPPORTED, "k1 does not fit on an SM");
   const int64_t units1 = (int64_t)dmax * (I / 8);
-  const int grid1 = (int)std::min<int64_t>((units1 + g1 - 1) / g1, (int64_t)sms * occ1);
+  const int grid1 = (int)std::min<int64_t>(units1, (int64_t)sms * occ1);
   int rc = fnx::launch_moe_up(a, NT, grid1, smem1, st);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no k1 instance");
   if (rc) return cuda_fail("MoE k1 launch");
 
   a.W = w2;
-  a.G = g2;
-  a.pdl = 1;  // k2 always overlaps its weight prefetch with k1's tail
-  const int occ2 = fnx::moe_down_occupancy(NT, cpw2, w2 * g2 * 32, smem2);
+  a.CPW = cpw2;
+  a.RT = rt2;
+  a.NS = ns2;
+  a.pdl = 1;  // k2 streams W2 while k1 drains
+  const size_t smem2 = geo.smem2;
+  const int occ2 = fnx::moe_down_occupancy(NT, cpw2, (w2 + 2) * 32, smem2);
   if (occ2 <= 0) return fail(FNX_EUNSUPPORTED, "k2 does not fit on an SM");
-  const int64_t units2 = (int64_t)dmax * (H / 16);
-  const int grid2 = (int)std::min<int64_t>((units2 + g2 - 1) / g2, (int64_t)sms * occ2);
+  const int64_t units2 = (int64_t)dmax * (H / (16 * rt2));
+  const int grid2 = (int)std::min<int64_t>(units2, (int64_t)sms * occ2);
   rc = fnx::launch_moe_down(a, NT, grid2, smem2, st);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no k2 instance");
   if (rc) return cuda_fail("MoE k2 launch");

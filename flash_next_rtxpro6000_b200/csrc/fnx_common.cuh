@@ -408,13 +408,125 @@ __device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrow
   }
 }
 
-// Ring of S register stages holding the weight loads of upcoming work units.
-template <int CPW, int S>
-struct WeightRing {
-  uint4 va[S][CPW];
-  uint4 vb[S][CPW];
-  uint32_t sa[S][CPW];
-  uint32_t sb[S][CPW];
-};
+// ------------------------------------------------------------------------------------
+// Asynchronous pipeline primitives: mbarriers and bulk (TMA) copies into shared memory.
+// Every wait is bounded: after kWaitLimitNs of polling it reports failure, and the
+// caller records an error code and leaves its loop instead of spinning forever.
+// ------------------------------------------------------------------------------------
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+enum ErrCode : int { ERR_NONE = 0, ERR_WAIT_FULL = 1, ERR_WAIT_EMPTY = 2, ERR_WAIT_RED = 3,
+                     ERR_WAIT_RFREE = 4, ERR_DRAIN = 5 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Arrive once and announce `bytes` of bulk-copy transactions for the current phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait until the phase with the given parity has completed; false after the time limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_test(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// Bulk copy global -> this CTA's shared memory, completing `bytes` on the mbarrier.
+// dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+// Asynchronous 4/8/16-byte global -> shared copies (cp.async) whose completion this
+// thread later hands to an mbarrier with cp_async_arrive (one arrival, counted in the
+// barrier's expected count).  Source and destination must be aligned to the size.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void record_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// ------------------------------------------------------------------------------------
+// Shared-memory tile layout.  A 16-row weight tile is stored as two halves of 8 rows
+// (physical rows 0..7 and 8..15), each at a row pitch of UB bytes, the second half
+// starting `tile_half_offset(UB)` bytes in; a half is one contiguous bulk copy when the
+// rows are contiguous in global memory.  The eight lanes of one 128-bit load phase hold
+// MMA rows g0 and g0 + 1 (g0 even); lanes with an odd g read the other half (MMA row g is
+// physical row g + 8 and vice versa), and the half offset puts the two rows of a phase
+// 64 bytes apart modulo 128, so the phase touches eight distinct bank groups.
+// ------------------------------------------------------------------------------------
+__host__ __device__ constexpr int tile_half_offset(int ub) {
+  return 8 * ub + ((64 - (ub % 128)) % 128 + 128) % 128;
+}
+__host__ __device__ constexpr int tile_bytes(int ub) {
+  return ((tile_half_offset(ub) + 8 * ub) + 127) / 128 * 128;
+}
+// Physical row of MMA row g (0..7) and of MMA row g + 8, for the lane's g.
+__device__ __forceinline__ int phys_lo(int g) { return (g & 1) ? g + 8 : g; }
+__device__ __forceinline__ int phys_hi(int g) { return (g & 1) ? g : g + 8; }
+__device__ __forceinline__ int tile_row_offset(int r, int ub) {
+  return r < 8 ? r * ub : tile_half_offset(ub) + (r - 8) * ub;
+}
 
 }  // namespace fnx

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "fnx_common.cuh"
+
 namespace fnx {
 
 struct DenseArgs {
@@ -28,15 +30,70 @@ struct DenseArgs {
   int64_t* am_out;              // [M] argmax row (global row id), or null
   unsigned long long* am_key_out;  // [M] raw argmax key copy (sharded heads), or null
   int64_t row_offset;           // global id of local row 0 (vocab shards)
-  float* ws;              // split-K partials [row_tiles * ksplit * 256]
-  unsigned int* ws_cnt;   // split-K counters [row_tiles] (zero between calls)
+  float* ws;              // split-K partials [tile_groups * ksplit * RT * 256]
+  unsigned int* ws_cnt;   // split-K counters [tile_groups] (zero between calls)
+  int* err;               // device error flag (first error code wins), or null
   int M, N, K;            // N = output columns (fused SiLU: H, weight rows 2H)
-  int ksplit;
+  int ksplit;             // k splits of a tile group (separate work units)
   int silu;
-  int W, G;               // warps per group, groups per CTA
-  int row_tiles, n_units;
+  int W;                  // consumer warps per CTA
+  int RT;                 // 16-row tiles per work unit
+  int NS;                 // shared-memory stages in the weight ring
+  int RS;                 // reduction slots between consumers and the epilogue warp
+  int UB;                 // weight bytes per row per unit
+  int TILE;               // shared-memory bytes of one 16-row tile (tile_bytes(UB))
+  int E;                  // epilogue warps (units alternate between them)
+  int nch_u;              // 64-byte chunks per row per unit
+  int row_tiles;          // 16-row (SiLU: 8-output) tiles
+  int tile_groups;        // ceil(row_tiles / RT)
+  int n_units;            // tile_groups * ksplit
   int pdl;
 };
+
+// One stage of the dense weight ring: RT tiles of weights, then the unit's row scales
+// (RT * 16 values, raw bf16 or fp32), then (NVFP4) the unit's e4m3 block scales,
+// RT * 16 rows of sbr bytes.
+struct DenseStage {
+  int rsoff, bsoff, sbr, bytes;
+};
+
+__host__ __device__ inline int dense_align(int v, int a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline DenseStage dense_stage(int nvfp4, int RT, int tile, int nch_u) {
+  DenseStage d;
+  d.rsoff = RT * tile;
+  d.bsoff = d.rsoff + RT * 64;
+  d.sbr = dense_align(nch_u * 8, 16);
+  d.bytes = dense_align(d.bsoff + (nvfp4 ? RT * 16 * d.sbr : 0), 128);
+  return d;
+}
+
+// Shared-memory layout of the dense kernel (host and device use the same function).
+struct DenseLayout {
+  int bars, stages, xs, unscale, red, sred, total;
+};
+
+__host__ __device__ inline DenseLayout dense_layout(int M, int K, int W, int NS, int RS, int NT,
+                                                    int stage_bytes) {
+  DenseLayout L;
+  int off = 0;
+  L.bars = off;
+  off = dense_align(off + (2 * NS + 2 * RS) * 8, 128);
+  L.stages = off;
+  off += NS * stage_bytes;
+  L.xs = dense_align(off, 128);
+  off = L.xs + M * (2 * K + 64);
+  L.unscale = dense_align(off, 16);
+  off = L.unscale + 16 * 4;
+  L.red = dense_align(off, 16);
+  off = L.red + RS * W * 32 * NT * 16;
+  L.sred = off;                       // per slot: 64 floats of row scales (RT x 16)
+  off += RS * 64 * 4;
+  L.total = dense_align(off, 128);
+  return L;
+}
+
+constexpr int kDenseThreadsMax = 20 * 32;  // producer + up to 3 epilogue + 16 consumer warps
 
 struct MoeArgs {
   const void* x;          // bf16 [M, H] hidden states (row stride ldx elements)
@@ -63,19 +120,74 @@ struct MoeArgs {
   int has_shared;
   int swizzled;           // block scales in the 128x4 swizzled layout (server format)
   // expert slice owned by this launch (expert-parallel shards): ids outside
-  // [e_lo, e_lo + E_local) are skipped; weight tensors hold the local experts only.
+  // [e_lo, e_lo + E) are skipped; weight tensors hold the local experts only.
   int e_lo;
-  // scratch
-  void* act;              // bf16 [M * (R + 1), I]
-  float* part;            // fp32 [M * (R + 1), H]
-  unsigned int* cnt;      // [H / 16] (zero between calls)
+  // scratch (caller-owned; counters zero between calls)
+  void* act;              // bf16 [M * (R + 1), I]            k1 -> k1 finaliser
+  uint8_t* act_f16;       // [dcap * 16] rows of 2I + 64 B     k1 finaliser -> k2 (B rows),
+                          //   row d * 16 + s = route slot s of distinct expert d
+  float* pair_unscale;    // [dcap * 16]                       inverse power of two per route
+  unsigned int* ecnt;     // [min(E, M*R) + 1]                 k1 units done per expert
+  float* part;            // fp32 [M * (R + 1), H]             k2 route partials
+  unsigned int* cnt;      // [H / 64]                          k2 experts done per row group
+  int* err;
   // output: bf16 [M, H] (or fp32 partial sums when out_f32, for cross-rank reduction)
   void* out;
   int64_t ldo;
   int out_f32;
-  int W, G;
+  // launch geometry (RT: 16-row tiles per k2 unit)
+  int W, CPW, NS, RS, NT, RT;
   int pdl;
 };
+
+// Shared-memory layout of the MoE kernels.
+struct MoeLayout {
+  int bars, stages, xs, unscale, red, ids, bitmap, wbase, exp_of, cnt_of, ent, misc, total;
+  int stage_bytes, wpitch, bpitch, brow0;  // stage: weight rows then B rows (k2)
+};
+
+constexpr int kMoeSlotCap = 16;  // routes of one distinct expert handled by one unit
+
+__host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/, int M, int R,
+                                                int E, int H, int I, int W, int NS, int RS,
+                                                int NT, int RT) {
+  MoeLayout L;
+  const int nw = (E + 31) / 32;
+  const int dcap = (E < M * R ? E : M * R) + 1;
+  const int ub = (kernel == 1 ? H : I) / 2;
+  L.wpitch = tile_bytes(ub);            // bytes of one 16-row tile
+  const int tiles = kernel == 1 ? 1 : RT;
+  L.bpitch = 2 * I + 64;
+  L.brow0 = tiles * L.wpitch;
+  L.stage_bytes = dense_align(L.brow0 + (kernel == 2 ? 8 * NT * L.bpitch : 0), 128);
+  int off = 0;
+  L.bars = off;
+  off = dense_align(off + (2 * NS + 2 * RS) * 8, 128);
+  L.stages = off;
+  off += NS * L.stage_bytes;
+  L.xs = off;
+  off += kernel == 1 ? M * (2 * H + 64) : 0;
+  L.unscale = dense_align(off, 16);
+  off = L.unscale + 16 * 4;
+  L.red = dense_align(off, 16);
+  off = L.red + RS * W * 32 * NT * 16 + RS * 64 * 4;  // partial tiles, then 64 floats/slot
+  L.ids = off;
+  off += dense_align(M * R, 4) * 4;
+  L.bitmap = off;
+  off += dense_align(nw, 4) * 4;
+  L.wbase = off;
+  off += dense_align(nw, 4) * 4;
+  L.exp_of = off;
+  off += dense_align(dcap, 4) * 4;
+  L.cnt_of = off;
+  off += dense_align(dcap, 4) * 4;
+  L.ent = off;
+  off += dense_align(dcap * kMoeSlotCap * 2, 16);
+  L.misc = off;
+  off += 16;
+  L.total = dense_align(off, 128);
+  return L;
+}
 
 int launch_dense(const DenseArgs& a, int wtype, int nt, int cpw, int grid, size_t smem,
                  cudaStream_t stream);
@@ -87,8 +199,6 @@ int launch_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
 int dense_occupancy(int wtype, int nt, int cpw, int threads, size_t smem);
 int moe_up_occupancy(int nt, int cpw, int threads, size_t smem);
 int moe_down_occupancy(int nt, int cpw, int threads, size_t smem);
-size_t moe_up_smem(int M, int R, int E, int H, int W, int G, int NT);
-size_t moe_down_smem(int M, int R, int E, int I, int W, int G, int NT);
 
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();

@@ -11,21 +11,27 @@
 //   w13 block scales e4m3 [E, 2I, H/16], 128x4 swizzled (or linear);
 //   g13 = w13_weight_scale_2[e, 0] for both halves; w2 [E, H, I/2], scales, g2[e].
 //
-// Routing table.  Every CTA decodes topk_ids itself (a 512-bit expert bitmap, a prefix
-// count, and per distinct expert the list of routes that chose it, in route order),
-// which costs a few hundred cycles and no extra launch.  Each distinct expert's rows are
-// then streamed ONCE for all tokens routed to it: the tokens are the B operand of the
+// Routing table.  Every CTA decodes topk_ids itself (an expert bitmap, a prefix count,
+// and per distinct expert the list of routes that chose it, in route order), which
+// costs a few hundred cycles and no extra launch.  Each distinct expert's rows are then
+// streamed ONCE for all tokens routed to it: the tokens are the B operand of the
 // tensor-core MMA, so verify widths cost D distinct experts, not M * top_k routes.
 // Route ids < 0 (and ids outside this launch's expert slice) are skipped
 // (0112-...patch:205, :259).
 //
+// Both kernels are persistent and warp-specialised like the dense GEMV: warp 0 bulk-
+// copies the unit's weight rows (and, in k2, its B rows) into a shared-memory ring,
+// warps 2.. dequantise + MMA, warp 1 runs the epilogue.
+//
 // k1 unit: (distinct expert, 8 columns of I): MMA rows 0..7 are up rows, 8..15 the
-// matching gate rows, so one lane holds both and applies silu(gate * g) * (up * g)
-// (0112-...patch:220-224) before rounding act to bf16.
-// k2 unit: (distinct expert, 16 rows of H): contribution = <W2 row, act> * (g2 * w_r)
+// matching gate rows, so one epilogue lane holds both and applies
+// silu(gate * g) * (up * g) (0112-...patch:220-224), rounding act to bf16.  The last k1
+// unit of an expert to finish converts that expert's act rows to fp16 scaled by a
+// per-route power of two, in the B-fragment layout, for k2 to bulk-copy.
+// k2 unit: (distinct expert, 16 * RT rows of H, RT <= 4): contribution = <W2 row, act> * (g2 * w_r)
 // (0112-...patch:268-269) written as an fp32 partial per (token, route); the last unit
-// to finish a row tile sums each token's routes in route order (then the shared expert)
-// and rounds once to bf16: deterministic, no float atomics.
+// to finish a 64-row group sums each token's routes in route order (then the shared
+// expert) and rounds once to bf16: deterministic, no float atomics.
 #include "fnx_common.cuh"
 #include "fnx_kernels.h"
 
@@ -33,46 +39,7 @@ namespace fnx {
 
 namespace {
 
-constexpr int kSlotCap = 16;  // routes per distinct expert handled by one unit (M <= 16)
-
-struct MoeSmem {
-  int xs, unscale, red, flags, ids, bitmap, wbase, exp_of, cnt_of, ent, misc, total;
-};
-
-__host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
-
-// Shared-memory layout of both MoE kernels.  `rows` staged rows of `K` elements.
-__host__ __device__ inline MoeSmem moe_smem_layout(int rows, int K, int M, int R, int E, int W,
-                                                   int G, int NT) {
-  MoeSmem s;
-  const int nw = (E + 31) / 32;
-  const int dcap = (E < M * R ? E : M * R) + 1;
-  int off = 0;
-  s.xs = off;
-  off += rows * stage_row_bytes(K);
-  s.unscale = off;
-  off += align_up(rows, 4) * 4;
-  s.red = off;
-  off += G * 2 * W * 32 * NT * 16;
-  s.flags = off;
-  off += align_up(G, 4) * 4;
-  s.ids = off;
-  off += align_up(M * R, 4) * 4;
-  s.bitmap = off;
-  off += align_up(nw, 4) * 4;
-  s.wbase = off;
-  off += align_up(nw, 4) * 4;
-  s.exp_of = off;
-  off += align_up(dcap, 4) * 4;
-  s.cnt_of = off;
-  off += align_up(dcap, 4) * 4;
-  s.ent = off;
-  off += align_up(dcap * kSlotCap * 2, 16);
-  s.misc = off;
-  off += 16;
-  s.total = off;
-  return s;
-}
+constexpr int kSlotCap = kMoeSlotCap;
 
 struct Routing {
   int* ids;          // [M*R] local expert id or -1
@@ -84,7 +51,7 @@ struct Routing {
   int* misc;         // misc[0] = D (distinct routed experts)
 };
 
-__device__ inline Routing routing_view(uint8_t* smem, const MoeSmem& L) {
+__device__ inline Routing routing_view(uint8_t* smem, const MoeLayout& L) {
   Routing r;
   r.ids = reinterpret_cast<int*>(smem + L.ids);
   r.bitmap = reinterpret_cast<uint32_t*>(smem + L.bitmap);
@@ -132,7 +99,6 @@ __device__ void route_decode(const MoeArgs& a, const Routing& rt) {
     if (lane == 0) rt.misc[0] = running;
   }
   __syncthreads();
-  // Distinct experts in ascending id order.
   for (int w = tid; w < nw; w += nthreads) {
     uint32_t m = rt.bitmap[w];
     int d = rt.wbase[w];
@@ -143,7 +109,6 @@ __device__ void route_decode(const MoeArgs& a, const Routing& rt) {
     }
   }
   __syncthreads();
-  // Route list of every distinct expert, in route order (one warp per expert).
   const int D = rt.misc[0];
   for (int d = warp; d < D; d += nwarps) {
     const int e = rt.exp_of[d];
@@ -171,158 +136,285 @@ __device__ __forceinline__ int64_t scale_offset(int swizzled, int row, int kb, i
          ((row & 127) >> 5) * 4 + (kb & 3);
 }
 
+// Routes of the unit's expert: count, and the route entry (t * R + r) of slot s.
+struct UnitRoutes {
+  int n;           // live B columns (<= 8 * NT)
+  bool shared;
+  int d;
+};
+
+__device__ __forceinline__ int slot_entry(const Routing& rt, const UnitRoutes& ur, int s) {
+  return ur.shared ? -1 - s : rt.ent[ur.d * kSlotCap + s];  // shared: -1 - token
+}
+
+__device__ __forceinline__ int pair_of(int entry, int R) {
+  if (entry < 0) {  // shared expert: token -1 - entry, route slot R
+    const int t = -1 - entry;
+    return t * (R + 1) + R;
+  }
+  return entry + entry / R;  // t * (R + 1) + r
+}
+
+__device__ __forceinline__ int token_of(int entry, int R) {
+  return entry < 0 ? -1 - entry : entry / R;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------
 // k1: act[t*(R+1)+r, j] = bf16(silu(g * <gate_j, x_t>) * g * <up_j, x_t>)
 // ------------------------------------------------------------------------------------
-template <int NT, int CPW, int S>
-__global__ void __launch_bounds__(512, 1) moe_up_kernel(const MoeArgs a) {
+template <int NT, int CPW>
+__global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int Q = Geo<W_NVFP4>::Q;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int W = a.W;
-  const int grp = warp / W, wig = warp - grp * W;
-  const int gthreads = W * 32, gtid = tid - grp * gthreads;
-  const int g = lane >> 2, c = lane & 3;
-  const int M = a.M, R = a.R, H = a.H, I = a.I;
-  const MoeSmem L = moe_smem_layout(M, H, M, R, a.E, W, a.G, NT);
+  const int M = a.M, R = a.R, H = a.H, I = a.I, W = a.W, NS = a.NS, RS = a.RS;
+  const MoeLayout L = moe_layout(1, M, R, a.E, H, I, W, NS, RS, NT, 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + NS;
+  uint64_t* rfull = empty + NS;
+  uint64_t* rfree = rfull + RS;
+  uint8_t* stages = smem + L.stages;
   uint8_t* xs = smem + L.xs;
   float* unscale = reinterpret_cast<float*>(smem + L.unscale);
   float* red = reinterpret_cast<float*>(smem + L.red);
+  float* sred = red + RS * W * 32 * NT * 4;
   const Routing rt = routing_view(smem, L);
   const int srow = stage_row_bytes(H);
   const int KP = H / 16;
-  const uint64_t pol = policy_evict_first();
+  const int UB = H / 2;
+  const int g = lane >> 2, c = lane & 3;
+  const int pg = phys_lo(g), pg8 = phys_hi(g);
+  const int bpitch = 2 * I + 64;
 
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    for (int r = 0; r < RS; ++r) {
+      mbar_init(&rfull[r], W);
+      mbar_init(&rfree[r], 1);
+    }
+    mbar_fence_init();
+  }
   // x and topk_ids come from earlier kernels.
   pdl_wait();
-  route_decode(a, rt);
+  route_decode(a, rt);  // ends with __syncthreads (also publishes the barrier inits)
   const int D = rt.misc[0];
   const int tiles = I / 8;
   const int n_units = (D + a.has_shared) * tiles;
-  const int stride = gridDim.x * a.G;
-  const int first = blockIdx.x * a.G + grp;
+  const int stride = gridDim.x, first = blockIdx.x;
+  const int my_units = first < n_units ? (n_units - first + stride - 1) / stride : 0;
 
-  auto expert_ptrs = [&](int d, const uint8_t*& wq, const uint8_t*& sf) {
-    if (d < D) {
-      const int e = rt.exp_of[d];
-      wq = a.w13 + (size_t)e * (2 * I) * (H / 2);
-      sf = a.s13 + (size_t)e * (2 * I) * KP;
-    } else {
-      wq = a.sh_w13;
-      sf = a.sh_s13;
-    }
+  auto unit_routes = [&](int u) {
+    UnitRoutes ur;
+    ur.d = u / tiles;
+    ur.shared = ur.d >= D;
+    const int n = ur.shared ? M : rt.cnt_of[ur.d];
+    ur.n = n < 8 * NT ? n : 8 * NT;
+    return ur;
   };
+  auto expert_w = [&](int d) -> const uint8_t* {
+    return d < D ? a.w13 + (size_t)rt.exp_of[d] * (2 * I) * UB : a.sh_w13;
+  };
+  auto expert_s = [&](int d) -> const uint8_t* {
+    return d < D ? a.s13 + (size_t)rt.exp_of[d] * (2 * I) * KP : a.sh_s13;
+  };
+  // weight row of physical row r: 0..7 up rows, 8..15 the matching gate rows
+  auto wrow = [&](int tile, int r) { return r < 8 ? tile * 8 + r : I + tile * 8 + (r - 8); };
 
-  WeightRing<CPW, S> ring;
-  auto load = [&](int u, uint4(&va)[CPW], uint4(&vb)[CPW], uint32_t(&sa)[CPW],
-                  uint32_t(&sb)[CPW]) {
+  auto issue = [&](int i) {
+    const uint64_t pol = policy_evict_first();
+    const int u = first + i * stride;
+    const int s = i % NS;
     const int d = u / tiles, tile = u - d * tiles;
-    const uint8_t *wq, *sf;
-    expert_ptrs(d, wq, sf);
-    const int ra = tile * 8 + g;      // up row
-    const int rb = I + tile * 8 + g;  // gate row
-#pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int chunk = wig * CPW + cc;
-      const int off = chunk * 64 + c * 16;
-      va[cc] = ldg_stream(wq + (size_t)ra * (H / 2) + off, pol);
-      vb[cc] = ldg_stream(wq + (size_t)rb * (H / 2) + off, pol);
-      const int kb = chunk * 8 + c * 2;
-      sa[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, ra, kb, KP), pol);
-      sb[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, rb, kb, KP), pol);
-    }
+    const uint8_t* wq = expert_w(d);
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(16 * UB));
+    __syncwarp();
+    if (lane < 2)  // two contiguous 8-row blocks: up rows, gate rows
+      bulk_g2s(stages + (size_t)s * L.stage_bytes + tile_row_offset(8 * lane, UB),
+               wq + (size_t)wrow(tile, 8 * lane) * UB, (uint32_t)(8 * UB), &full[s], pol);
   };
 
-  auto process = [&](int u, const uint4(&va)[CPW], const uint4(&vb)[CPW],
-                     const uint32_t(&sa)[CPW], const uint32_t(&sb)[CPW], int it) {
-    const int d = u / tiles, tile = u - d * tiles;
-    const bool shared = d >= D;
-    const int n_e = shared ? M : rt.cnt_of[d];
-    // Token of B column slot (nt * 8 + g).
-    int tok[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int s = nt * 8 + g;
-      tok[nt] = (s < n_e) ? (shared ? s : rt.ent[d * kSlotCap + s] / R) : -1;
-    }
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
-#pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int chunk = wig * CPW + cc;
-      uint4 xf[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          xf[nt][q] = (tok[nt] >= 0)
-                          ? *reinterpret_cast<const uint4*>(xs + (size_t)tok[nt] * srow +
-                                                            ((chunk * 4 + q) * 4 + c) * 16)
-                          : make_uint4(0u, 0u, 0u, 0u);
-      chunk_mma<W_NVFP4, NT>(acc, va[cc], vb[cc], sa[cc], sb[cc], xf, n_e > 8 ? 2 : 1);
-    }
-    float* rbuf = red + (size_t)((grp * 2 + (it & 1)) * W) * 32 * NT * 4;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      *reinterpret_cast<float4*>(rbuf + ((size_t)(wig * 32 + lane) * NT + nt) * 4) =
-          make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    group_sync(1 + grp, gthreads);
-
-    // gtid = slot * 16 + i; rows 0..7 up, 8..15 gate (gthreads >= 256).
-    const int slot = gtid >> 4, i = gtid & 15;
-    const bool live = slot < n_e;
-    float rowsum = 0.f;
-    if (live) {
-      const int nt = slot >> 3, col = slot & 7;
-      const int src = (i & 7) * 4 + (col >> 1);
-      const int reg = ((i >> 3) << 1) | (col & 1);
-      for (int w = 0; w < W; ++w) rowsum += rbuf[((size_t)(w * 32 + src) * NT + nt) * 4 + reg];
-    }
-    const float gate = __shfl_down_sync(0xffffffffu, rowsum, 8);
-    if (live && i < 8) {
-      int t, pair;
-      if (shared) {
-        t = slot;
-        pair = t * (R + 1) + R;
-      } else {
-        const int entry = rt.ent[d * kSlotCap + slot];
-        t = entry / R;
-        pair = entry + t;
-      }
-      const float gs = shared ? __ldg(a.sh_g13) : __ldg(a.g13 + (size_t)rt.exp_of[d] * a.g13_stride);
-      const float us = unscale[t];
-      const float upv = rowsum * us * gs;
-      const float gv = gate * us * gs;
-      reinterpret_cast<__nv_bfloat16*>(a.act)[(size_t)pair * I + tile * 8 + i] =
-          __float2bfloat16_rn(silu_f32(gv) * upv);
-    }
-  };
-
-#pragma unroll
-  for (int s = 0; s < S - 1; ++s) {
-    const int u = first + s * stride;
-    if (u < n_units) load(u, ring.va[s], ring.vb[s], ring.sa[s], ring.sb[s]);
+  if (warp == 0) {
+    const int pre = my_units < NS ? my_units : NS;
+    for (int i = 0; i < pre; ++i) issue(i);
   }
   stage_rows<W_NVFP4>(xs, unscale, M, H, [&](int r) {
     return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
   });
   __syncthreads();
 
-  int it = 0;
-  for (int base = first; base < n_units; base += S * stride) {
+  if (warp == 0) {
+    int issued = my_units < NS ? my_units : NS;
+    for (int i = NS; i < my_units; ++i) {
+      if (!mbar_wait(&empty[i % NS], ((i / NS) & 1) ^ 1)) {
+        record_error(a.err, ERR_WAIT_EMPTY);
+        break;
+      }
+      issue(i);
+      issued = i + 1;
+    }
+    for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+      if (!mbar_wait(&full[j % NS], (j / NS) & 1)) record_error(a.err, ERR_DRAIN);
+  } else if (warp >= 2) {
+    const int cw = warp - 2;  // k slice of the unit
+    const uint64_t pol = policy_evict_first();
+    uint32_t sa[CPW], sb[CPW], na[CPW], nb[CPW];
+    float gsc = 0.f, ngsc = 0.f;
+    auto prefetch = [&](int i, uint32_t(&xa)[CPW], uint32_t(&xb)[CPW], float& gs) {
+      const int u = first + i * stride;
+      const int d = u / tiles, tile = u - d * tiles;
+      const uint8_t* sf = expert_s(d);
+      const int ra = wrow(tile, pg), rb = wrow(tile, pg8);
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int u = base + s * stride;
-      if (u >= n_units) break;
-      const int un = u + (S - 1) * stride;
-      const int nxt = (s + S - 1) % S;
-      if (un < n_units) load(un, ring.va[nxt], ring.vb[nxt], ring.sa[nxt], ring.sb[nxt]);
-      process(u, ring.va[s], ring.vb[s], ring.sa[s], ring.sb[s], it);
-      ++it;
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int kb = (cw * CPW + cc) * 8 + c * 2;
+        xa[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, ra, kb, KP), pol);
+        xb[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, rb, kb, KP), pol);
+      }
+      if (cw == 0 && lane == 0)
+        gs = d < D ? __ldg(a.g13 + (size_t)rt.exp_of[d] * a.g13_stride) : __ldg(a.sh_g13);
+    };
+    if (my_units > 0) prefetch(0, sa, sb, gsc);
+    for (int i = 0; i < my_units; ++i) {
+      const int u = first + i * stride;
+      const UnitRoutes ur = unit_routes(u);
+      if (i + 1 < my_units) prefetch(i + 1, na, nb, ngsc);
+      int tok[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int sl = nt * 8 + g;
+        tok[nt] = sl < ur.n ? token_of(slot_entry(rt, ur, sl), R) : -1;
+      }
+      const int s = i % NS;
+      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+        record_error(a.err, ERR_WAIT_FULL);
+        break;
+      }
+      const uint8_t* st = stages + (size_t)s * L.stage_bytes;
+      const uint8_t* rowa = st + tile_row_offset(pg, UB) + c * 16;
+      const uint8_t* rowb = st + tile_row_offset(pg8, UB) + c * 16;
+      float acc[2][NT][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[h][nt][r] = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int ch = cw * CPW + cc;
+        const uint4 va = lds128(rowa + ch * 64);
+        const uint4 vb = lds128(rowb + ch * 64);
+        uint4 xf[NT][Q];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int q = 0; q < Q; ++q)
+            xf[nt][q] = tok[nt] >= 0
+                            ? lds128(xs + (size_t)tok[nt] * srow + ((ch * Q + q) * 4 + c) * 16)
+                            : make_uint4(0u, 0u, 0u, 0u);
+        chunk_mma<W_NVFP4, NT>(acc[cc & 1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      const int rs = i % RS;
+      if (!mbar_wait(&rfree[rs], ((i / RS) & 1) ^ 1)) {
+        record_error(a.err, ERR_WAIT_RFREE);
+        break;
+      }
+      float* dst = red + ((size_t)(rs * W + cw) * 32 + lane) * NT * 4;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float4*>(dst + nt * 4) =
+            make_float4(acc[0][nt][0] + acc[1][nt][0], acc[0][nt][1] + acc[1][nt][1],
+                        acc[0][nt][2] + acc[1][nt][2], acc[0][nt][3] + acc[1][nt][3]);
+      if (cw == 0 && lane == 0) sred[rs * 64] = gsc;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfull[rs]);
+#pragma unroll
+      for (int cc = 0; cc < CPW; ++cc) {
+        sa[cc] = na[cc];
+        sb[cc] = nb[cc];
+      }
+      gsc = ngsc;
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    for (int i = 0; i < my_units; ++i) {
+      const int u = first + i * stride;
+      const UnitRoutes ur = unit_routes(u);
+      const int tile = u - ur.d * tiles;
+      const int rs = i % RS;
+      if (!mbar_wait(&rfull[rs], (i / RS) & 1)) {
+        record_error(a.err, ERR_WAIT_RED);
+        break;
+      }
+      const float gs = sred[rs * 64];
+      float v[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < W; ++w) {
+          const float4 p =
+              *reinterpret_cast<const float4*>(red + ((size_t)(rs * W + w) * 32 + lane) * NT * 4 + nt * 4);
+          sum.x += p.x;
+          sum.y += p.y;
+          sum.z += p.z;
+          sum.w += p.w;
+        }
+        v[nt][0] = sum.x;
+        v[nt][1] = sum.y;
+        v[nt][2] = sum.z;
+        v[nt][3] = sum.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfree[rs]);
+      // MMA row g is physical row pg: the up row of column g for even g, the gate row
+      // for odd g; MMA row g + 8 is the other one.
+      const bool odd = g & 1;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int sl = nt * 8 + 2 * c + p;
+          if (sl >= ur.n) continue;
+          const int entry = slot_entry(rt, ur, sl);
+          const int t = token_of(entry, R);
+          const float us = unscale[t];
+          const float upv = (odd ? v[nt][2 + p] : v[nt][p]) * us * gs;
+          const float gv = (odd ? v[nt][p] : v[nt][2 + p]) * us * gs;
+          reinterpret_cast<__nv_bfloat16*>(a.act)[(size_t)pair_of(entry, R) * I + tile * 8 + g] =
+              __float2bfloat16_rn(silu_f32(gv) * upv);
+        }
+      // The last unit of this expert converts its act rows into k2's B-operand rows
+      // (expert-contiguous: row d * 16 + slot).
+      __threadfence();
+      __syncwarp();
+      unsigned prev = 0;
+      if (lane == 0) prev = atomicAdd(&a.ecnt[ur.d], 1u);
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      if (prev == (unsigned)(tiles - 1)) {
+        __threadfence();
+        for (int sl = 0; sl < ur.n; ++sl) {
+          const int pair = pair_of(slot_entry(rt, ur, sl), R);
+          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.act) + (size_t)pair * I;
+          float m = 0.f;
+          for (int k8 = lane; k8 < I / 8; k8 += 32) m = fmaxf(m, bf16x8_absmax(ldg_cg_u4(src + 8 * k8)));
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          const int e = stage_exponent(m);
+          uint8_t* dst = a.act_f16 + (size_t)(ur.d * kSlotCap + sl) * bpitch;
+          for (int k8 = lane; k8 < I / 8; k8 += 32)
+            *reinterpret_cast<uint4*>(dst + stage_unit_offset<W_NVFP4>(8 * k8)) =
+                bf16x8_to_f16x8_scaled(ldg_cg_u4(src + 8 * k8), e);
+          if (lane == 0) a.pair_unscale[ur.d * kSlotCap + sl] = pow2f(-e);
+        }
+        if (lane == 0) a.ecnt[ur.d] = 0u;
+      }
     }
   }
   pdl_trigger();
@@ -331,33 +423,50 @@ __global__ void __launch_bounds__(512, 1) moe_up_kernel(const MoeArgs a) {
 // ------------------------------------------------------------------------------------
 // k2: out[t, n] = sum_r w_{t,r} * g2_{e_r} * <W2[e_r, n], act_{t,r}>  (+ shared expert)
 // ------------------------------------------------------------------------------------
-template <int NT, int CPW, int S>
-__global__ void __launch_bounds__(512, 1) moe_down_kernel(const MoeArgs a) {
+template <int NT, int CPW>
+__global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_down_kernel(const MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int Q = Geo<W_NVFP4>::Q;
+  constexpr int kMaxRT = 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int W = a.W;
-  const int grp = warp / W, wig = warp - grp * W;
-  const int gthreads = W * 32, gtid = tid - grp * gthreads;
-  const int g = lane >> 2, c = lane & 3;
-  const int M = a.M, R = a.R, H = a.H, I = a.I;
-  const int P = M * (R + 1);
-  const MoeSmem L = moe_smem_layout(P, I, M, R, a.E, W, a.G, NT);
-  uint8_t* xs = smem + L.xs;
-  float* unscale = reinterpret_cast<float*>(smem + L.unscale);
+  const int M = a.M, R = a.R, H = a.H, I = a.I, W = a.W, NS = a.NS, RS = a.RS;
+  const int RT = a.RT;  // 16-row tiles per unit (16 * RT rows of H)
+  const int KSL = W / RT;
+  const MoeLayout L = moe_layout(2, M, R, a.E, H, I, W, NS, RS, NT, RT);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + NS;
+  uint64_t* rfull = empty + NS;
+  uint64_t* rfree = rfull + RS;
+  uint8_t* stages = smem + L.stages;
   float* red = reinterpret_cast<float*>(smem + L.red);
-  int* flags = reinterpret_cast<int*>(smem + L.flags);
+  float* sred = red + RS * W * 32 * NT * 4;
   const Routing rt = routing_view(smem, L);
-  const int srow = stage_row_bytes(I);
   const int KP = I / 16;
-  const uint64_t pol = policy_evict_first();
+  const int UB = I / 2;
+  const int g = lane >> 2, c = lane & 3;
+  const int pg = phys_lo(g), pg8 = phys_hi(g);
 
-  // topk_ids were written before k1 started and k1 triggers this launch only after its
-  // own wait, so they are visible here; act (k1's output) is read after pdl_wait().
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    for (int r = 0; r < RS; ++r) {
+      mbar_init(&rfull[r], W);
+      mbar_init(&rfree[r], 1);
+    }
+    mbar_fence_init();
+  }
+  // topk_ids were written before k1 started, and k1 lets this grid launch only after
+  // its own griddepcontrol.wait, so they are visible here; act_f16 is read after
+  // this kernel's pdl_wait().
   route_decode(a, rt);
   const int D = rt.misc[0];
   const int Dtot = D + a.has_shared;
-  const int tiles = H / 16;
-  const int n_units = Dtot * tiles;
+  const int groups = H / (16 * RT);
+  const int n_units = Dtot * groups;
+  const int stride = gridDim.x, first = blockIdx.x;
+  const int my_units = first < n_units ? (n_units - first + stride - 1) / stride : 0;
   if (Dtot == 0) {  // every route skipped: the layer output is zero
     pdl_wait();
     for (int o = blockIdx.x * blockDim.x + tid; o < M * H; o += gridDim.x * blockDim.x) {
@@ -370,170 +479,256 @@ __global__ void __launch_bounds__(512, 1) moe_down_kernel(const MoeArgs a) {
     pdl_trigger();
     return;
   }
-  const int stride = gridDim.x * a.G;
-  const int first = blockIdx.x * a.G + grp;
 
-  auto expert_ptrs = [&](int d, const uint8_t*& wq, const uint8_t*& sf) {
-    if (d < D) {
-      const int e = rt.exp_of[d];
-      wq = a.w2 + (size_t)e * H * (I / 2);
-      sf = a.s2 + (size_t)e * H * KP;
-    } else {
-      wq = a.sh_w2;
-      sf = a.sh_s2;
-    }
+  auto unit_routes = [&](int u) {
+    UnitRoutes ur;
+    ur.d = u / groups;
+    ur.shared = ur.d >= D;
+    const int n = ur.shared ? M : rt.cnt_of[ur.d];
+    ur.n = n < 8 * NT ? n : 8 * NT;
+    return ur;
+  };
+  auto expert_w = [&](int d) -> const uint8_t* {
+    return d < D ? a.w2 + (size_t)rt.exp_of[d] * H * UB : a.sh_w2;
+  };
+  auto expert_s = [&](int d) -> const uint8_t* {
+    return d < D ? a.s2 + (size_t)rt.exp_of[d] * H * KP : a.sh_s2;
   };
 
-  WeightRing<CPW, S> ring;
-  auto load = [&](int u, uint4(&va)[CPW], uint4(&vb)[CPW], uint32_t(&sa)[CPW],
-                  uint32_t(&sb)[CPW]) {
-    const int d = u / tiles, tile = u - d * tiles;
-    const uint8_t *wq, *sf;
-    expert_ptrs(d, wq, sf);
-    const int ra = tile * 16 + g, rb = ra + 8;
-#pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int chunk = wig * CPW + cc;
-      const int off = chunk * 64 + c * 16;
-      va[cc] = ldg_stream(wq + (size_t)ra * (I / 2) + off, pol);
-      vb[cc] = ldg_stream(wq + (size_t)rb * (I / 2) + off, pol);
-      const int kb = chunk * 8 + c * 2;
-      sa[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, ra, kb, KP), pol);
-      sb[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, rb, kb, KP), pol);
-    }
+  // Weight blocks of stage i (valid before k1 completes) and its B rows (after pdl_wait).
+  auto issue_weights = [&](int i, int brows) {
+    const uint64_t pol = policy_evict_first();
+    const int u = first + i * stride;
+    const int s = i % NS;
+    const int d = u / groups, grp = u - d * groups;
+    const uint8_t* wq = expert_w(d) + (size_t)grp * RT * 16 * UB;
+    if (lane == 0)
+      mbar_arrive_expect_tx(&full[s], (uint32_t)(RT * 16 * UB + brows * L.bpitch));
+    __syncwarp();
+    if (lane < 2 * RT)  // tile lane/2, half lane%2: 8 contiguous rows
+      bulk_g2s(stages + (size_t)s * L.stage_bytes + (lane >> 1) * L.wpitch +
+                   tile_row_offset(8 * (lane & 1), UB),
+               wq + (size_t)(lane * 8) * UB, (uint32_t)(8 * UB), &full[s], pol);
+  };
+  auto issue_brows = [&](int i) {
+    const uint64_t pol = policy_evict_first();
+    const int u = first + i * stride;
+    const int s = i % NS;
+    const UnitRoutes ur = unit_routes(u);
+    if (lane == 0 && ur.n > 0)
+      bulk_g2s(stages + (size_t)s * L.stage_bytes + L.brow0,
+               a.act_f16 + (size_t)(ur.d * kSlotCap) * L.bpitch, (uint32_t)(ur.n * L.bpitch),
+               &full[s], pol);
   };
 
-  auto process = [&](int u, const uint4(&va)[CPW], const uint4(&vb)[CPW],
-                     const uint32_t(&sa)[CPW], const uint32_t(&sb)[CPW], int it) {
-    const int d = u / tiles, tile = u - d * tiles;
-    const bool shared = d >= D;
-    const int n_e = shared ? M : rt.cnt_of[d];
-    int prow[NT];  // staged act row (pair id) of B column slot nt*8+g
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int s = nt * 8 + g;
-      if (s >= n_e) {
-        prow[nt] = -1;
-      } else if (shared) {
-        prow[nt] = s * (R + 1) + R;
-      } else {
-        const int entry = rt.ent[d * kSlotCap + s];
-        prow[nt] = entry + entry / R;
+  const int pre = my_units < NS ? my_units : NS;
+  if (warp == 0)
+    for (int i = 0; i < pre; ++i) issue_weights(i, unit_routes(first + i * stride).n);
+  pdl_wait();
+  __syncthreads();
+
+  if (warp == 0) {
+    for (int i = 0; i < pre; ++i) issue_brows(i);
+    int issued = pre;
+    for (int i = NS; i < my_units; ++i) {
+      if (!mbar_wait(&empty[i % NS], ((i / NS) & 1) ^ 1)) {
+        record_error(a.err, ERR_WAIT_EMPTY);
+        break;
       }
+      issue_weights(i, unit_routes(first + i * stride).n);
+      issue_brows(i);
+      issued = i + 1;
     }
-    float acc[NT][4];
+    for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+      if (!mbar_wait(&full[j % NS], (j / NS) & 1)) record_error(a.err, ERR_DRAIN);
+  } else if (warp >= 2) {
+    const int cw = warp - 2;
+    const int rtile = cw / KSL, kq = cw - rtile * KSL;
+    const bool factor_warp = cw == 0;  // hands the unit's per-route factors over
+    const uint64_t pol = policy_evict_first();
+    uint32_t sa[CPW], sb[CPW], na[CPW], nb[CPW];
+    float fac = 0.f, nfac = 0.f;
+    auto prefetch = [&](int i, uint32_t(&xa)[CPW], uint32_t(&xb)[CPW], float& f) {
+      const int u = first + i * stride;
+      const int d = u / groups, grp = u - d * groups;
+      const uint8_t* sf = expert_s(d);
+      const int base = (grp * RT + rtile) * 16;
+      const int ra = base + pg, rb = base + pg8;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int kb = (kq * CPW + cc) * 8 + c * 2;
+        xa[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, ra, kb, KP), pol);
+        xb[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, rb, kb, KP), pol);
+      }
+      if (factor_warp) {  // lane s: factor of route slot s = act unscale * g2 * weight
+        const UnitRoutes ur = unit_routes(u);
+        if (lane < ur.n) {
+          const int entry = slot_entry(rt, ur, lane);
+          const float g2 = d < D ? __ldg(a.g2 + (size_t)rt.exp_of[d] * a.g2_stride) : __ldg(a.sh_g2);
+          const float wr = entry < 0 ? 1.f : __ldg(a.wts + entry);
+          f = __ldcg(a.pair_unscale + d * kSlotCap + lane) * (g2 * wr);
+        }
+      }
+    };
+    if (my_units > 0) prefetch(0, sa, sb, fac);
+    for (int i = 0; i < my_units; ++i) {
+      const int u = first + i * stride;
+      const UnitRoutes ur = unit_routes(u);
+      if (i + 1 < my_units) prefetch(i + 1, na, nb, nfac);
+      const int s = i % NS;
+      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+        record_error(a.err, ERR_WAIT_FULL);
+        break;
+      }
+      const uint8_t* st = stages + (size_t)s * L.stage_bytes;
+      const uint8_t* wst = st + (size_t)rtile * L.wpitch;
+      const uint8_t* rowa = wst + tile_row_offset(pg, UB) + c * 16;
+      const uint8_t* rowb = wst + tile_row_offset(pg8, UB) + c * 16;
+      const uint8_t* bst = st + L.brow0;
+      float acc[2][NT][4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int chunk = wig * CPW + cc;
-      uint4 xf[NT][4];
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[h][nt][r] = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int ch = kq * CPW + cc;
+        const uint4 va = lds128(rowa + ch * 64);
+        const uint4 vb = lds128(rowb + ch * 64);
+        uint4 xf[NT][Q];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int sl = nt * 8 + g;
+#pragma unroll
+          for (int q = 0; q < Q; ++q)
+            xf[nt][q] = sl < ur.n ? lds128(bst + (size_t)sl * L.bpitch + ((ch * Q + q) * 4 + c) * 16)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+        }
+        chunk_mma<W_NVFP4, NT>(acc[cc & 1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      const int rs = i % RS;
+      if (!mbar_wait(&rfree[rs], ((i / RS) & 1) ^ 1)) {
+        record_error(a.err, ERR_WAIT_RFREE);
+        break;
+      }
+      float* dst = red + ((size_t)(rs * W + cw) * 32 + lane) * NT * 4;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float4*>(dst + nt * 4) =
+            make_float4(acc[0][nt][0] + acc[1][nt][0], acc[0][nt][1] + acc[1][nt][1],
+                        acc[0][nt][2] + acc[1][nt][2], acc[0][nt][3] + acc[1][nt][3]);
+      if (factor_warp && lane < ur.n) sred[rs * 64 + lane] = fac;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfull[rs]);
+#pragma unroll
+      for (int cc = 0; cc < CPW; ++cc) {
+        sa[cc] = na[cc];
+        sb[cc] = nb[cc];
+      }
+      fac = nfac;
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    for (int i = 0; i < my_units; ++i) {
+      const int u = first + i * stride;
+      const UnitRoutes ur = unit_routes(u);
+      const int grp = u - ur.d * groups;
+      const int rs = i % RS;
+      if (!mbar_wait(&rfull[rs], (i / RS) & 1)) {
+        record_error(a.err, ERR_WAIT_RED);
+        break;
+      }
+      float sc[NT][2];
+      int pr[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          xf[nt][q] = (prow[nt] >= 0)
-                          ? *reinterpret_cast<const uint4*>(xs + (size_t)prow[nt] * srow +
-                                                            ((chunk * 4 + q) * 4 + c) * 16)
-                          : make_uint4(0u, 0u, 0u, 0u);
-      chunk_mma<W_NVFP4, NT>(acc, va[cc], vb[cc], sa[cc], sb[cc], xf, n_e > 8 ? 2 : 1);
-    }
-    float* rbuf = red + (size_t)((grp * 2 + (it & 1)) * W) * 32 * NT * 4;
+        for (int p = 0; p < 2; ++p) {
+          const int sl = nt * 8 + 2 * c + p;
+          const bool live = sl < ur.n;
+          pr[nt][p] = live ? pair_of(slot_entry(rt, ur, sl), R) : -1;
+          sc[nt][p] = live ? sred[rs * 64 + sl] : 0.f;
+        }
+      float v[kMaxRT][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      *reinterpret_cast<float4*>(rbuf + ((size_t)(wig * 32 + lane) * NT + nt) * 4) =
-          make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    group_sync(1 + grp, gthreads);
-
-    const float g2 = shared ? __ldg(a.sh_g2) : __ldg(a.g2 + (size_t)rt.exp_of[d] * a.g2_stride);
-    for (int o = gtid; o < 16 * n_e; o += gthreads) {
-      const int slot = o >> 4, i = o & 15;
-      const int nt = slot >> 3, col = slot & 7;
-      const int src = (i & 7) * 4 + (col >> 1);
-      const int reg = ((i >> 3) << 1) | (col & 1);
-      float rowsum = 0.f;
-      for (int w = 0; w < W; ++w) rowsum += rbuf[((size_t)(w * 32 + src) * NT + nt) * 4 + reg];
-      int pair;
-      float wr;
-      if (shared) {
-        pair = slot * (R + 1) + R;
-        wr = 1.f;
-      } else {
-        const int entry = rt.ent[d * kSlotCap + slot];
-        pair = entry + entry / R;
-        wr = __ldg(a.wts + entry);
+      for (int r4 = 0; r4 < kMaxRT; ++r4) {
+        if (r4 >= RT) break;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int kq = 0; kq < KSL; ++kq) {
+            const float4 p = *reinterpret_cast<const float4*>(
+                red + ((size_t)(rs * W + r4 * KSL + kq) * 32 + lane) * NT * 4 + nt * 4);
+            sum.x += p.x;
+            sum.y += p.y;
+            sum.z += p.z;
+            sum.w += p.w;
+          }
+          v[r4][nt][0] = sum.x;
+          v[r4][nt][1] = sum.y;
+          v[r4][nt][2] = sum.z;
+          v[r4][nt][3] = sum.w;
+        }
       }
-      st_cg_f32(a.part + (size_t)pair * H + tile * 16 + i, rowsum * unscale[pair] * (g2 * wr));
-    }
-    __threadfence();
-    group_sync(1 + grp, gthreads);
-    if (gtid == 0) {
-      const unsigned prev = atomicAdd(&a.cnt[tile], 1u);
-      flags[grp] = (prev == (unsigned)(Dtot - 1));
-    }
-    group_sync(1 + grp, gthreads);
-    if (!flags[grp]) return;
-    __threadfence();
-    for (int o = gtid; o < 16 * M; o += gthreads) {
-      const int t = o >> 4, i = o & 15;
-      const int n = tile * 16 + i;
-      float s = 0.f;
-      for (int r = 0; r < R; ++r)
-        if (rt.ids[t * R + r] >= 0) s += ld_cg_f32(a.part + (size_t)(t * (R + 1) + r) * H + n);
-      if (a.has_shared) s += ld_cg_f32(a.part + (size_t)(t * (R + 1) + R) * H + n);
-      if (a.out_f32)
-        reinterpret_cast<float*>(a.out)[(size_t)t * a.ldo + n] = s;
-      else
-        reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.ldo + n] = __float2bfloat16_rn(s);
-    }
-    if (gtid == 0) a.cnt[tile] = 0u;  // all Dtot arrivals for this tile have happened
-  };
-
-  // W2 does not depend on k1: start streaming it before waiting for act.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfree[rs]);
 #pragma unroll
-  for (int s = 0; s < S - 1; ++s) {
-    const int u = first + s * stride;
-    if (u < n_units) load(u, ring.va[s], ring.vb[s], ring.sa[s], ring.sb[s]);
-  }
-  pdl_wait();
-  stage_rows<W_NVFP4>(xs, unscale, P, I, [&](int p) -> const __nv_bfloat16* {
-    const int t = p / (R + 1), r = p - t * (R + 1);
-    const bool used = (r == R) ? (a.has_shared != 0) : (rt.ids[t * R + r] >= 0);
-    return used ? reinterpret_cast<const __nv_bfloat16*>(a.act) + (size_t)p * I : nullptr;
-  });
-  __syncthreads();
-
-  int it = 0;
-  for (int base = first; base < n_units; base += S * stride) {
+      for (int r4 = 0; r4 < kMaxRT; ++r4) {
+        if (r4 >= RT) break;
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int u = base + s * stride;
-      if (u >= n_units) break;
-      const int un = u + (S - 1) * stride;
-      const int nxt = (s + S - 1) % S;
-      if (un < n_units) load(un, ring.va[nxt], ring.vb[nxt], ring.sa[nxt], ring.sb[nxt]);
-      process(u, ring.va[s], ring.vb[s], ring.sa[s], ring.sb[s], it);
-      ++it;
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            if (pr[nt][p] < 0) continue;
+            float* dst = a.part + (size_t)pr[nt][p] * H + (grp * RT + r4) * 16;
+            st_cg_f32(dst + pg, v[r4][nt][p] * sc[nt][p]);
+            st_cg_f32(dst + pg8, v[r4][nt][2 + p] * sc[nt][p]);
+          }
+      }
+      __threadfence();
+      __syncwarp();
+      unsigned prev = 0;
+      if (lane == 0) prev = atomicAdd(&a.cnt[grp], 1u);
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      if (prev == (unsigned)(Dtot - 1)) {
+        // every expert of this 64-row group is in: sum each token's routes in route
+        // order, then the shared expert, round once
+        __threadfence();
+        for (int o = lane; o < M * RT * 16; o += 32) {
+          const int t = o / (RT * 16), n = grp * RT * 16 + (o - t * RT * 16);
+          float sum = 0.f;
+          for (int r = 0; r < R; ++r)
+            if (rt.ids[t * R + r] >= 0) sum += ld_cg_f32(a.part + (size_t)(t * (R + 1) + r) * H + n);
+          if (a.has_shared) sum += ld_cg_f32(a.part + (size_t)(t * (R + 1) + R) * H + n);
+          if (a.out_f32)
+            reinterpret_cast<float*>(a.out)[(size_t)t * a.ldo + n] = sum;
+          else
+            reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.ldo + n] = __float2bfloat16_rn(sum);
+        }
+        if (lane == 0) a.cnt[grp] = 0u;
+      }
     }
   }
   pdl_trigger();
 }
 
+namespace {
+
 using MoeKernel = void (*)(const MoeArgs);
 
 MoeKernel moe_up_ptr(int nt, int cpw) {
-  if (nt == 1) return cpw == 1 ? moe_up_kernel<1, 1, 4> : (cpw == 2 ? moe_up_kernel<1, 2, 3> : nullptr);
-  if (nt == 2) return cpw == 1 ? moe_up_kernel<2, 1, 4> : (cpw == 2 ? moe_up_kernel<2, 2, 3> : nullptr);
+  if (nt == 1) return cpw == 1 ? moe_up_kernel<1, 1> : cpw == 2 ? moe_up_kernel<1, 2> : cpw == 4 ? moe_up_kernel<1, 4> : nullptr;
+  if (nt == 2) return cpw == 1 ? moe_up_kernel<2, 1> : cpw == 2 ? moe_up_kernel<2, 2> : cpw == 4 ? moe_up_kernel<2, 4> : nullptr;
   return nullptr;
 }
 
 MoeKernel moe_down_ptr(int nt, int cpw) {
-  if (nt == 1)
-    return cpw == 1 ? moe_down_kernel<1, 1, 4> : (cpw == 2 ? moe_down_kernel<1, 2, 3> : nullptr);
-  if (nt == 2)
-    return cpw == 1 ? moe_down_kernel<2, 1, 4> : (cpw == 2 ? moe_down_kernel<2, 2, 3> : nullptr);
+  if (nt == 1) return cpw == 1 ? moe_down_kernel<1, 1> : cpw == 2 ? moe_down_kernel<1, 2> : cpw == 4 ? moe_down_kernel<1, 4> : nullptr;
+  if (nt == 2) return cpw == 1 ? moe_down_kernel<2, 1> : cpw == 2 ? moe_down_kernel<2, 2> : cpw == 4 ? moe_down_kernel<2, 4> : nullptr;
   return nullptr;
 }
 
@@ -544,12 +739,7 @@ int occupancy_of(MoeKernel k, int threads, size_t smem) {
   return n;
 }
 
-size_t moe_up_smem(int M, int R, int E, int H, int W, int G, int NT) {
-  return (size_t)moe_smem_layout(M, H, M, R, E, W, G, NT).total;
-}
-size_t moe_down_smem(int M, int R, int E, int I, int W, int G, int NT) {
-  return (size_t)moe_smem_layout(M * (R + 1), I, M, R, E, W, G, NT).total;
-}
+}  // namespace
 
 int moe_up_occupancy(int nt, int cpw, int threads, size_t smem) {
   return occupancy_of(moe_up_ptr(nt, cpw), threads, smem);
@@ -558,25 +748,18 @@ int moe_down_occupancy(int nt, int cpw, int threads, size_t smem) {
   return occupancy_of(moe_down_ptr(nt, cpw), threads, smem);
 }
 
-// CPW is fixed by the shapes: k1 streams H / 128 chunks over W warps, k2 I / 128.
 int launch_moe_up(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream) {
-  const int chunks = a.H / 128;
-  const int cpw = chunks / a.W;
-  if (cpw * a.W != chunks) return 1;
-  MoeKernel k = moe_up_ptr(nt, cpw);
+  MoeKernel k = moe_up_ptr(nt, a.CPW);
   if (!k) return 1;
   if (!prepare_kernel((const void*)k)) return 2;
-  return launch_with_pdl((const void*)k, a, grid, a.W * a.G * 32, smem, a.pdl, stream);
+  return launch_with_pdl((const void*)k, a, grid, (a.W + 2) * 32, smem, a.pdl, stream);
 }
 
 int launch_moe_down(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream) {
-  const int chunks = a.I / 128;
-  const int cpw = chunks / a.W;
-  if (cpw * a.W != chunks) return 1;
-  MoeKernel k = moe_down_ptr(nt, cpw);
+  MoeKernel k = moe_down_ptr(nt, a.CPW);
   if (!k) return 1;
   if (!prepare_kernel((const void*)k)) return 2;
-  return launch_with_pdl((const void*)k, a, grid, a.W * a.G * 32, smem, a.pdl, stream);
+  return launch_with_pdl((const void*)k, a, grid, (a.W + 2) * 32, smem, a.pdl, stream);
 }
 
 }  // namespace fnx

@@ -25,7 +25,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import FnxMoeWeights, FnxMoeWorkspace, check, ptr
+from ._lib import FnxMoeWeights, FnxMoeWorkspace, FnxMoeWorkspaceSizes, check, ptr
 from .w8a16_gemv import _activation, _stream
 
 logger = logging.getLogger(__name__)
@@ -48,15 +48,25 @@ DEFAULT_CONFIG = DraftMoeGemvConfig()
 
 @dataclass(frozen=True)
 class DraftMoeWorkspace:
-    act: torch.Tensor        # [max_tokens * (R + 1), I] bf16, k1 -> k2
-    partials: torch.Tensor   # [max_tokens * (R + 1), H] fp32 route partials of k2
-    counters: torch.Tensor   # [H / 16] int32, zero between launches (self-resetting)
+    """Scratch of one MoE layer call.  Counters are zero between launches (every launch
+    leaves them at zero), so nothing is cleared per call or graph replay."""
+
+    act: torch.Tensor              # [P, I] bf16 activation, P = max_tokens * (R + 1)
+    act_f16: torch.Tensor          # uint8 rows of 2I + 64 B: act in the down kernel's B layout,
+                                   # row d * 16 + s = route slot s of distinct expert d
+    pair_unscale: torch.Tensor     # fp32 per-route inverse power of two, same indexing
+    expert_counters: torch.Tensor  # [min(E, max_tokens * R) + 1] int32
+    partials: torch.Tensor         # [P, H] fp32 route partials of the down kernel
+    counters: torch.Tensor         # [H / 16] int32
+    error_flag: torch.Tensor       # [1] int32 device error code (0 = none)
     max_tokens: int
     num_routes: int
 
     def to_c(self) -> FnxMoeWorkspace:
-        return FnxMoeWorkspace(ptr(self.act), ptr(self.partials), ptr(self.counters),
-                               self.max_tokens, self.num_routes)
+        return FnxMoeWorkspace(ptr(self.act), ptr(self.act_f16), ptr(self.pair_unscale),
+                               ptr(self.expert_counters), ptr(self.partials),
+                               ptr(self.counters), ptr(self.error_flag), self.max_tokens,
+                               self.num_routes)
 
 
 @dataclass
@@ -72,32 +82,53 @@ class SharedExpert:
 
 
 def unsupported_reason(*, hidden_size: int, intermediate_size: int,
-                       cfg: DraftMoeGemvConfig = DEFAULT_CONFIG) -> Optional[str]:
-    """Why these shapes cannot take the GEMV, or None (0112-...patch:289-304)."""
+                       cfg: DraftMoeGemvConfig = DEFAULT_CONFIG, num_routes: int = 10,
+                       num_experts: int = 512) -> Optional[str]:
+    """Why these shapes cannot take the GEMV, or None (0112-...patch:289-304).
+
+    The structural checks below are the library's; the last one asks the library
+    whether both kernels fit in shared memory at ``cfg.max_tokens`` tokens."""
     if hidden_size % _SF_TILE_ROWS or intermediate_size % _SF_TILE_ROWS:
         return "H and I must be multiples of 128 (no swizzle padding)"
     if (hidden_size // _FP4_BLOCK) % _SF_COL_GROUP or (intermediate_size // _FP4_BLOCK) % _SF_COL_GROUP:
         return "H/16 and I/16 must be multiples of 4 (no swizzle padding)"
     ch1, ch2 = hidden_size // 128, intermediate_size // 128
-    if not (8 <= ch1 <= 16 or (ch1 % 2 == 0 and 8 <= ch1 // 2 <= 16)):
-        return f"H={hidden_size}: the gate/up kernel tiles H in 8..32 chunks of 128"
-    if not (ch2 <= 16 or (ch2 % 2 == 0 and ch2 // 2 <= 16)):
-        return f"I={intermediate_size}: the down kernel tiles I in at most 32 chunks of 128"
+    # gate/up: the consumer warps split H into ch1 chunks of 128 (8..16 warps x 1..4 chunks)
+    if not any(ch1 % c == 0 and 4 <= ch1 // c <= 16 for c in (1, 2, 4)):
+        return f"H={hidden_size}: no gate/up tiling (H/128 must be 4..16 warps x 1, 2 or 4 chunks)"
+    # down: rt row tiles (rt <= 4, 16 * rt dividing H) x (ch2 / c) k slices <= 16 warps
+    if not any(hidden_size % (16 * rt) == 0 and ch2 % c == 0 and rt * (ch2 // c) <= 16
+               for rt in (1, 2, 3, 4) for c in (1, 2, 4)):
+        return f"I={intermediate_size}: no down tiling (I/128 must split into <= 16 slices)"
     if cfg.max_tokens < 1 or cfg.max_tokens > _lib.MAX_M:
         return "max_tokens must be in [1, 16]"
+    sz = FnxMoeWorkspaceSizes()
+    if _lib.lib().fnx_moe_workspace_bytes(cfg.max_tokens, num_routes, num_experts, hidden_size,
+                                          intermediate_size, ctypes.byref(sz)) != _lib.FNX_OK:
+        return _lib.last_error()
     return None
 
 
 def make_workspace(*, num_routes: int, hidden_size: int, intermediate_size: int,
                    device: torch.device, cfg: DraftMoeGemvConfig = DEFAULT_CONFIG,
-                   max_tokens: Optional[int] = None) -> DraftMoeWorkspace:
+                   max_tokens: Optional[int] = None,
+                   num_experts: int = 4096) -> DraftMoeWorkspace:
     """Scratch of one MoE layer call (0112-...patch:307-325), sized for max_tokens."""
     m = cfg.max_tokens if max_tokens is None else max_tokens
+    sz = FnxMoeWorkspaceSizes()
+    check(_lib.lib().fnx_moe_workspace_bytes(m, num_routes, num_experts, hidden_size,
+                                             intermediate_size, ctypes.byref(sz)),
+          "make_workspace")
     pairs = m * (num_routes + 1)
+    u8 = dict(dtype=torch.uint8, device=device)
     return DraftMoeWorkspace(
         act=torch.empty((pairs, intermediate_size), dtype=torch.bfloat16, device=device),
+        act_f16=torch.empty(sz.act_f16, **u8),
+        pair_unscale=torch.empty(sz.pair_unscale // 4, dtype=torch.float32, device=device),
+        expert_counters=torch.zeros(sz.expert_counters // 4, dtype=torch.int32, device=device),
         partials=torch.empty((pairs, hidden_size), dtype=torch.float32, device=device),
-        counters=torch.zeros(hidden_size // 16, dtype=torch.int32, device=device),
+        counters=torch.zeros(sz.counters // 4, dtype=torch.int32, device=device),
+        error_flag=torch.zeros(1, dtype=torch.int32, device=device),
         max_tokens=m, num_routes=num_routes,
     )
 

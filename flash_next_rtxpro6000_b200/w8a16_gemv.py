@@ -45,7 +45,9 @@ PDL = _env_flag("FNX_PDL")
 
 @dataclass(frozen=True)
 class GemvConfig:
-    """Launch geometry (see include/fnx_gemv.h fnx_gemv_cfg)."""
+    """Launch geometry (see include/fnx_gemv.h fnx_gemv_cfg): `warps` consumer warps,
+    each streaming `chunks_per_warp` 64-byte chunks of every row of one of `groups`
+    16-row tiles per unit; `ksplit` k splits; `grid` CTAs (0 = one persistent wave)."""
 
     warps: int
     chunks_per_warp: int
@@ -66,8 +68,10 @@ class Workspace:
         self.counters = torch.zeros(_WS_COUNTERS, dtype=torch.int32, device=device)
         self.argmax_keys = torch.zeros(_lib.MAX_M, dtype=torch.int64, device=device)
         self.argmax_count = torch.zeros(1, dtype=torch.int32, device=device)
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=device)
         self.c = FnxWorkspace(ptr(self.partials), _WS_FLOATS, ptr(self.counters), _WS_COUNTERS,
-                              ptr(self.argmax_keys), ptr(self.argmax_count))
+                              ptr(self.argmax_keys), ptr(self.argmax_count),
+                              ptr(self.error_flag))
 
 
 class scratch_slot:

@@ -70,12 +70,17 @@ typedef struct fnx_workspace {
   int64_t n_counters;
   unsigned long long* argmax_keys; /* FNX_MAX_M keys                              */
   unsigned int* argmax_count;      /* one CTA arrival counter                     */
+  int* error_flag;                 /* device error code (0 = none), or NULL: a wait
+                                      that exceeded its time limit records its code */
 } fnx_workspace;
 
-/* Optional launch geometry override (NULL = built-in planner).  warps: warps sharing
- * one 16-row tile; chunks_per_warp: 64-byte row chunks each warp streams per tile (1, 2
- * or 4); groups: tiles in flight per CTA; ksplit: k splits across CTAs; grid: CTAs
- * (0 = persistent, one wave). */
+/* Optional launch geometry override (NULL = built-in planner).  A work unit is
+ * `groups` 16-row tiles x (K / ksplit).  warps: consumer warps per CTA (<= 16);
+ * chunks_per_warp: 64-byte row chunks each consumer streams per unit (1, 2, 4 or 8);
+ * groups: 16-row tiles per unit (1..4, dividing warps); ksplit: k splits (separate
+ * units, summed by the last split); grid: CTAs (0 = one persistent wave).
+ * (warps / groups) * chunks_per_warp * ksplit must equal K / chunk, chunk = 64 B of a row
+ * (64 k for int8/fp8, 32 for bf16, 128 for NVFP4). */
 typedef struct fnx_gemv_cfg {
   int warps;
   int chunks_per_warp;
@@ -160,16 +165,24 @@ typedef struct fnx_moe_weights {
 } fnx_moe_weights;
 
 typedef struct fnx_moe_workspace {
-  void* act;             /* bf16 [M * (R + 1), I]                 */
-  float* partials;       /* fp32 [M * (R + 1), H]                 */
-  unsigned int* counters;/* [H / 16], zero when first used         */
-  int max_m;             /* capacity the buffers were sized for    */
+  void* act;                     /* bf16 [P, I], P = max_m * (max_routes + 1)          */
+  void* act_f16;                 /* [P, 2I + 64] bytes: act in the k2 B-operand layout  */
+  float* pair_unscale;           /* [P] per-route inverse power of two                  */
+  unsigned int* expert_counters; /* [min(E, max_m * max_routes) + 1], zero on first use */
+  float* partials;               /* fp32 [P, H]                                         */
+  unsigned int* counters;        /* [H / 64], zero on first use                         */
+  int* error_flag;               /* device error code, or NULL                          */
+  int max_m;                     /* capacity the buffers were sized for                 */
   int max_routes;
 } fnx_moe_workspace;
 
-/* Bytes of each fnx_moe_workspace buffer for (M, R, H, I). */
-int fnx_moe_workspace_bytes(int M, int R, int H, int I, int64_t* act_bytes,
-                            int64_t* partial_bytes, int64_t* counter_bytes);
+/* Byte sizes of the fnx_moe_workspace buffers for (max_m, max_routes, E, H, I). */
+typedef struct fnx_moe_workspace_sizes {
+  int64_t act, act_f16, pair_unscale, expert_counters, partials, counters;
+} fnx_moe_workspace_sizes;
+
+int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, int I,
+                            fnx_moe_workspace_sizes* out);
 
 /*
  * out[t, :] = sum_r topk_weights[t, r] * expert(topk_ids[t, r])(x[t]) [+ shared(x[t])]

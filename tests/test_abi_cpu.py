@@ -9,7 +9,8 @@ import re
 import pytest
 
 from flash_next_rtxpro6000_b200 import _lib
-from flash_next_rtxpro6000_b200._lib import FnxGemvCfg, FnxMoeWeights, FnxMoeWorkspace
+from flash_next_rtxpro6000_b200._lib import (FnxGemvCfg, FnxMoeWeights, FnxMoeWorkspace,
+                                             FnxMoeWorkspaceSizes)
 
 HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "fnx_gemv.h")
 
@@ -39,10 +40,10 @@ def test_planner_invariants(M, N, K, wt):
     c = FnxGemvCfg()
     assert _lib.lib().fnx_plan_gemv(M, N, K, wt, 0, 0, ctypes.byref(c)) == 0
     ch = {_lib.W_INT8: 64, _lib.W_FP8_E4M3: 64, _lib.W_BF16: 32, _lib.W_NVFP4: 128}[wt]
-    assert c.warps * c.chunks_per_warp * c.ksplit == K // ch
-    assert c.warps * 32 >= 16 * M
-    assert 1 <= c.groups <= 8 and c.warps * c.groups <= 16
-    assert c.chunks_per_warp in (1, 2, 4)
+    # groups = 16-row tiles per unit; warps / groups consumer warps share each tile's k
+    assert 1 <= c.groups <= 4 and c.warps % c.groups == 0 and c.warps <= 16
+    assert (c.warps // c.groups) * c.chunks_per_warp * c.ksplit == K // ch
+    assert c.chunks_per_warp in (1, 2, 4, 8)
     if N >= 49152:
         assert c.ksplit == 1  # the wide heads fill the machine on N alone
 
@@ -80,7 +81,7 @@ def test_zero_tokens_returns_ok_without_launch():
 def test_moe_validation():
     lib = _lib.lib()
     w = FnxMoeWeights(16, 16, 16, 2, 16, 16, 16, 1, 512, 0, 2000, 512, 1)
-    ws = FnxMoeWorkspace(16, 16, 16, 16, 10)
+    ws = FnxMoeWorkspace(16, 16, 16, 16, 16, 16, 16, 16, 10)
     rc = lib.fnx_moe_gemv(16, 2000, 16, 16, 1, 10, ctypes.byref(w), None, 16, 2000, 0,
                           ctypes.byref(ws), 0, None)
     assert rc == _lib.FNX_EUNSUPPORTED
@@ -95,7 +96,8 @@ def test_moe_validation():
 
 
 def test_moe_workspace_bytes():
-    a, p, c = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
-    assert _lib.lib().fnx_moe_workspace_bytes(16, 10, 2048, 512, ctypes.byref(a), ctypes.byref(p),
-                                              ctypes.byref(c)) == 0
-    assert (a.value, p.value, c.value) == (16 * 11 * 512 * 2, 16 * 11 * 2048 * 4, 128 * 4)
+    z = FnxMoeWorkspaceSizes()
+    assert _lib.lib().fnx_moe_workspace_bytes(16, 10, 512, 2048, 512, ctypes.byref(z)) == 0
+    P = 16 * 11
+    assert (z.act, z.act_f16, z.pair_unscale, z.expert_counters, z.partials, z.counters) == (
+        P * 512 * 2, 161 * 16 * (2 * 512 + 64), 161 * 16 * 4, 161 * 4, P * 2048 * 4, 128 * 4)

@@ -84,7 +84,8 @@ def test_config2_matches_oracle(M):
     assert rel_err(got, ref_dq) <= REL_TOL
     l2 = np.linalg.norm(got - ref) / np.linalg.norm(ref)
     assert l2 < 5e-3, l2
-    assert int(ws.counters.abs().sum()) == 0
+    assert int(ws.counters.abs().sum()) == 0 and int(ws.expert_counters.abs().sum()) == 0
+    assert int(ws.error_flag.item()) == 0
 
 
 def test_negative_ids_are_skipped_and_no_shared():
@@ -145,7 +146,7 @@ def test_deterministic_and_graph_replay(M):
     torch.cuda.synchronize()
     ref2 = _oracle(L, x2, ids2, wts2)
     assert rel_err(to_np(yg), ref2) <= REL_TOL
-    assert int(ws.counters.abs().sum()) == 0
+    assert int(ws.counters.abs().sum()) == 0 and int(ws.expert_counters.abs().sum()) == 0
     del g
 
 
