@@ -16,11 +16,13 @@ FNX_OK, FNX_EINVAL, FNX_ECUDA, FNX_EUNSUPPORTED = 0, 1, 2, 3
 W_INT8, W_FP8_E4M3, W_BF16, W_NVFP4 = 0, 1, 2, 3
 SCALE_NONE, SCALE_F32_SCALAR, SCALE_F32_ROW, SCALE_BF16_SCALAR, SCALE_BF16_ROW = 0, 1, 2, 3, 4
 MAX_M = 16
+STATIC_PARTIAL_FLOATS, STATIC_COUNTERS = 256 * 1024, 2048  # fnx_w8a16_gemv_static_ws limits
 
 EXPORTED = (
     "fnx_plan_gemv",
     "fnx_gemv_workspace_need",
     "fnx_w8a16_gemv",
+    "fnx_w8a16_gemv_static_ws",
     "fnx_w8a16_gemv_silu_mul",
     "fnx_w4a16_nvfp4_gemv",
     "fnx_moe_workspace_bytes",
@@ -111,6 +113,9 @@ def _declare(lib):
         _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, _P, c_int64, c_int64, c_int,
         _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int,
         _P]
+    lib.fnx_w8a16_gemv_static_ws.argtypes = [
+        _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, _P, c_int64, c_int64, c_int,
+        _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg), c_int, _P]
     lib.fnx_w8a16_gemv_silu_mul.argtypes = [
         _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, c_int, c_int, c_int,
         POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int, _P]

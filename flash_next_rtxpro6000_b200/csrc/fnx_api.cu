@@ -360,6 +360,39 @@ int moe_geometry(int M, int R, int E, int H, int I, MoeGeo& g) {
   return FNX_OK;
 }
 
+// ---- workspace-free variant ------------------------------------------------------
+// Some callers hold no device allocator of their own: a host program that binds the
+// C ABI directly (cgo, JNI, a ctypes script) owns the weights and activations it
+// passes in, but has no memory pool to carve a scratch buffer from for every shape.
+// For them the scratch lives in one static array per device, laid out as
+//   [0, 128)      argmax keys (16 x u64)        zero between calls
+//   [256, 260)    argmax counter (u32)          zero between calls
+//   [512, 516)    device error word (i32)
+//   [4096, ...)   split-K counters, then split-K partial floats (counters zero between calls)
+static __device__ __align__(256) unsigned char g_static_scratch[FNX_STATIC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {};
+
+// Address of the current device's array, resolved once per device.
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_fail("cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FNX_EUNSUPPORTED, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p)
+      return cuda_fail("cudaGetSymbolAddress(static scratch)");
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return FNX_OK;
+}
+}  // namespace
+
 extern "C" {
 
 int fnx_plan_gemv(int M, int N, int K, int w_dtype, int fused_silu, int argmax,
@@ -404,6 +437,43 @@ int fnx_w8a16_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, int w
   DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, y2, ldy2,
                  split_n, out_f32, argmax_out, argmax_key_out, row_offset, M, N, K, 0,
                  cfg, ws, pdl, static_cast<cudaStream_t>(stream)};
+  return run_dense(c);
+}
+
+int fnx_w8a16_gemv_static_ws(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                             int w_dtype, const void* scale, int scale_kind, void* y,
+                             int64_t ldy, void* y2, int64_t ldy2, int64_t split_n, int out_f32,
+                             int64_t* argmax_out, unsigned long long* argmax_key_out,
+                             int64_t row_offset, int M, int N, int K, const fnx_gemv_cfg* cfg,
+                             int pdl, fnx_stream_t stream) {
+  g_err.clear();
+  if (w_dtype != FNX_W_INT8 && w_dtype != FNX_W_FP8_E4M3 && w_dtype != FNX_W_BF16)
+    return fail(FNX_EINVAL, "fnx_w8a16_gemv_static_ws: w_dtype must be int8, fp8_e4m3 or bf16");
+  if (M < 1 || M > FNX_MAX_M) return fail(FNX_EINVAL, "M=%d must be in [1, 16]", M);
+  DensePlan p;
+  if (int rc = plan_dense(M, N, K, w_dtype, 0, cfg, p)) return rc;
+  const int64_t floats = p.ksplit > 1 ? (int64_t)p.tile_groups * p.ksplit * p.RT * 256 : 0;
+  const int64_t counters = p.ksplit > 1 ? p.tile_groups : 0;
+  if (floats > FNX_STATIC_PARTIAL_FLOATS || counters > FNX_STATIC_COUNTERS)
+    return fail(FNX_EUNSUPPORTED,
+                "static scratch too small: the plan needs %lld partial floats and %lld counters; "
+                "it holds %d and %d (use fnx_w8a16_gemv with a workspace)",
+                (long long)floats, (long long)counters, FNX_STATIC_PARTIAL_FLOATS,
+                FNX_STATIC_COUNTERS);
+  void* base = nullptr;
+  if (int rc = static_scratch(&base)) return rc;
+  unsigned char* b = static_cast<unsigned char*>(base);
+  fnx_workspace ws;
+  ws.argmax_keys = reinterpret_cast<unsigned long long*>(b);
+  ws.argmax_count = reinterpret_cast<unsigned int*>(b + 256);
+  ws.error_flag = reinterpret_cast<int*>(b + 512);
+  ws.counters = reinterpret_cast<unsigned int*>(b + 4096);
+  ws.n_counters = FNX_STATIC_COUNTERS;
+  ws.partials = reinterpret_cast<float*>(b + 4096 + 4 * FNX_STATIC_COUNTERS);
+  ws.partial_floats = FNX_STATIC_PARTIAL_FLOATS;
+  DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, y2, ldy2,
+                 split_n, out_f32, argmax_out, argmax_key_out, row_offset, M, N, K, 0,
+                 cfg, &ws, pdl, static_cast<cudaStream_t>(stream)};
   return run_dense(c);
 }
 

@@ -201,6 +201,33 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
 int fnx_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
                       fnx_stream_t stream);
 
+/*
+ * fnx_w8a16_gemv without a caller workspace: the argmax keys, split-K partials and
+ * counters live in one static device array of the library (FNX_STATIC_SCRATCH_BYTES
+ * per device), so the call allocates no device memory.  No counterpart in the
+ * reference, whose Triton launches allocate their scratch through torch.
+ *
+ * - Arguments and results are those of fnx_w8a16_gemv (ws omitted).
+ * - A plan whose split-K scratch exceeds FNX_STATIC_PARTIAL_FLOATS partial floats or
+ *   FNX_STATIC_COUNTERS counters is rejected with FNX_EUNSUPPORTED.
+ * - The first call on a device resolves the array's address (one-time setup with
+ *   that device current); make that first call before capturing a stream.
+ * - All calls on a device share the array: calls that may run at the same time
+ *   (different streams without ordering) race on it.  The argmax keys, the argmax
+ *   counter and the split-K counters must be zero when a call starts; they are zero
+ *   at load and every completed call leaves them zero.
+ * - A device-side wait that gives up records its code in the array's error word,
+ *   which this entry point does not report; fnx_w8a16_gemv with a workspace does.
+ */
+#define FNX_STATIC_PARTIAL_FLOATS (256 * 1024)
+#define FNX_STATIC_COUNTERS 2048
+#define FNX_STATIC_SCRATCH_BYTES (4096 + 4 * FNX_STATIC_COUNTERS + 4 * FNX_STATIC_PARTIAL_FLOATS)
+int fnx_w8a16_gemv_static_ws(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                             int w_dtype, const void* scale, int scale_kind, void* y,
+                             int64_t ldy, void* y2, int64_t ldy2, int64_t split_n, int out_f32,
+                             int64_t* argmax_out, unsigned long long* argmax_key_out,
+                             int64_t row_offset, int M, int N, int K, const fnx_gemv_cfg* cfg,
+                             int pdl, fnx_stream_t stream);
 /* Description of the last error of the calling thread ("" if none). */
 const char* fnx_last_error(void);
 
