@@ -9,23 +9,28 @@
 // Work decomposition.  A work unit is RT 16-row weight tiles (a SiLU tile is 8 gate rows
 // plus the matching 8 up rows) over the k range of one split.  Each persistent CTA runs
 // three roles:
-//   * warp 0, producer: one bulk copy (cp.async.bulk, mbarrier completion) per weight
-//     row into an NS-stage shared-memory ring, issued by the warp's lanes in parallel;
-//   * warps 2.., consumers: each takes one k slice of one row tile, reads its 64-byte
+//   * warp 0, producer: bulk copies (cp.async.bulk, mbarrier completion) of the unit's
+//     weight rows (two 8-row blocks per contiguous tile) and cp.async copies of its row
+//     scales and NVFP4 block scales into an NS-stage shared-memory ring, all completing
+//     on the stage's one mbarrier;
+//   * warps E+1 .., consumers: each takes one k slice of one row tile, reads its 64-byte
 //     chunks from the stage with conflict-free 128-bit loads, dequantises in registers
-//     and runs mma.sync on two independent accumulator chains; it then hands the
-//     partial tile to the epilogue through a double-buffered reduction slot;
-//   * warp 1, epilogue: sums the k slices in a fixed order, applies the per-token and
-//     per-row scales, rounds to bf16 (w8a16_gemv.py:92-95) and stores; with ksplit > 1
-//     it publishes the split's tile sums and the last split to arrive sums them in split
-//     order and resets the tile counter (w8a16_gemv.py:289-321).
-// Roles synchronise only through mbarriers (no CTA-wide barrier in the steady state) and
-// every wait is bounded (an expired wait records an error code and ends the role).
+//     and runs mma.sync on independent accumulator chains; it then hands the partial
+//     tile to an epilogue warp through a reduction slot;
+//   * warps 1 .. E, epilogue (units alternate between them): sum the k slices in a fixed
+//     order, apply the per-token and per-row scales, round to bf16 (w8a16_gemv.py:92-95)
+//     and store; with ksplit > 1 the split's tile sums are published and the last split
+//     to arrive sums them in split order and resets the tile counter
+//     (w8a16_gemv.py:289-321).
+// Roles synchronise only through mbarriers (no CTA-wide barrier in the steady state),
+// every wait is bounded (an expired wait records an error code and ends the role), and
+// unit positions advance without integer division.
 //
 // Greedy argmax (fused).  The epilogue builds a 64-bit key of each bf16-rounded logit
 // and its global row; the key maximum is the largest logit with the lowest row on ties
-// (torch.argmax).  Keys are reduced per tile with shuffles, per CTA in registers, across
-// CTAs with one atomicMax per token, and the last CTA decodes and clears them.
+// (torch.argmax).  Each lane keeps its running maximum per token in registers; at the
+// end the eight lanes of a token combine theirs with shuffles, each CTA does one
+// atomicMax per token, and the last CTA decodes and clears the keys.
 #include "fnx_common.cuh"
 #include "fnx_kernels.h"
 
@@ -101,11 +106,10 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
 
   // Producer: weights by bulk copy (two 8-row blocks per full contiguous tile, else a
   // copy per row), the unit's scales by cp.async; all complete on full[s].
-  auto issue = [&](int i) {
+  auto issue = [&](const UnitCursor& cu) {
     const uint64_t pol = policy_evict_first();
-    const int u = first + i * stride;
-    const int s = i % NS;
-    const int tg = u / ksplit, ks = u - tg * ksplit;
+    const int s = cu.s;
+    const int tg = cu.q, ks = cu.r;
     uint8_t* st = stages + (size_t)s * SG.bytes;
     if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(RT * 16 * UB));
     __syncwarp();
@@ -128,29 +132,31 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
         // 16 raw scales: 16 * esz bytes = esz chunks of 16 B (SiLU: 8 gate + 8 up values)
         const uint8_t* sbase = reinterpret_cast<const uint8_t*>(a.scale);
         if (lane < esz) {
-          const int half_chunks = esz / 2;  // 16-B chunks per 8 values
-          const int h = lane / half_chunks, j = lane - h * half_chunks;
+          // 16-B chunks per 8 values: one (bf16) or two (fp32)
+          const int h = esz == 2 ? lane : lane >> 1, j = esz == 2 ? 0 : lane & 1;
           const size_t first_val = silu ? (size_t)(h ? N + t * 8 : t * 8) : (size_t)t * 16 + 8 * h;
           cp_async16(st + SG.rsoff + rt * 64 + h * 8 * esz + j * 16, sbase + first_val * esz + j * 16);
         }
       }
       if constexpr (WT == W_NVFP4) {
         // e4m3 block scales of this unit's k range: nch_u * 8 bytes per row, 8 at a time
-        for (int idx = lane; idx < 16 * a.nch_u; idx += 32) {
-          const int r = idx / a.nch_u, j = idx - r * a.nch_u;
+        for (int r = 0; r < 16; ++r) {
           bool ok;
           const int row = row_of(t, r, ok);
-          cp_async8(st + SG.bsoff + (rt * 16 + r) * SG.sbr + j * 8,
-                    a.bs + (size_t)row * a.ldbs + (size_t)ks * a.nch_u * 8 + j * 8);
+          for (int j = lane; j < a.nch_u; j += 32)
+            cp_async8(st + SG.bsoff + (rt * 16 + r) * SG.sbr + j * 8,
+                      a.bs + (size_t)row * a.ldbs + (size_t)ks * a.nch_u * 8 + j * 8);
         }
       }
     }
     cp_async_arrive(&full[s]);
   };
 
+  UnitCursor pc;  // producer position
+  pc.init(first, stride, ksplit, NS);
   if (warp == 0) {
     const int pre = my_units < NS ? my_units : NS;
-    for (int i = 0; i < pre; ++i) issue(i);
+    for (int i = 0; i < pre; ++i, pc.next()) issue(pc);
   }
   // The weights and scales do not depend on the previous kernel; the activations may.
   pdl_wait();
@@ -162,12 +168,12 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     int issued = my_units < NS ? my_units : NS;
-    for (int i = NS; i < my_units; ++i) {
-      if (!mbar_wait(&empty[i % NS], ((i / NS) & 1) ^ 1)) {
+    for (int i = NS; i < my_units; ++i, pc.next()) {
+      if (!mbar_wait(&empty[pc.s], pc.ph ^ 1)) {
         record_error(a.err, ERR_WAIT_EMPTY);
         break;
       }
-      issue(i);
+      issue(pc);
       issued = i + 1;
     }
     // No copy may still be landing when the CTA exits.
@@ -178,12 +184,18 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
     const int cw = warp - 1 - E;
     const int rt = cw / KSL, kq = cw - rt * KSL;
     const bool scale_lane = per_row && (kq == 0) && (c == 0);  // hands the row scales over
-    for (int i = 0; i < my_units; ++i) {
-      const int u = first + i * stride;
-      const int tg = u / ksplit, ks = u - tg * ksplit;
+    const int offa = rt * TILE + tile_row_offset(pg, UB) + c * 16;
+    const int offb = rt * TILE + tile_row_offset(pg8, UB) + c * 16;
+    const int soffa = SG.bsoff + (rt * 16 + pg) * SG.sbr + c * 2;
+    const int soffb = SG.bsoff + (rt * 16 + pg8) * SG.sbr + c * 2;
+    UnitCursor cu;
+    cu.init(first, stride, ksplit, NS);
+    int rs = 0, rph = 0;  // reduction slot of this unit and its phase parity
+    for (int i = 0; i < my_units; ++i, cu.next()) {
+      const int tg = cu.q, ks = cu.r;
       const int t = tg * RT + rt;
-      const int s = i % NS;
-      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+      const int s = cu.s;
+      if (!mbar_wait(&full[s], cu.ph)) {
         record_error(a.err, ERR_WAIT_FULL);
         break;
       }
@@ -205,14 +217,14 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
           r1 = load_row_scale(a.scale, a.scale_kind, row_of(t, pg8, okb));
         }
       }
-      const uint8_t* wt = st + (size_t)rt * TILE;
-      const uint8_t* rowa = wt + tile_row_offset(pg, UB) + c * 16;
-      const uint8_t* rowb = wt + tile_row_offset(pg8, UB) + c * 16;
-      const uint8_t* sca = st + SG.bsoff + (rt * 16 + pg) * SG.sbr + c * 2;
-      const uint8_t* scb = st + SG.bsoff + (rt * 16 + pg8) * SG.sbr + c * 2;
-      float acc[2][NT][4];
+      const uint8_t* rowa = st + offa;
+      const uint8_t* rowb = st + offb;
+      const uint8_t* sca = st + soffa;
+      const uint8_t* scb = st + soffb;
+      constexpr int NC = NT == 1 ? 4 : 2;  // independent accumulator chains
+      float acc[NC][NT][4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < NC; ++h)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -237,27 +249,34 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
             xf[nt][q] = (tk < M) ? lds128(xs + (size_t)tk * srow + ((ch * Q + q) * 4 + c) * 16)
                                  : make_uint4(0u, 0u, 0u, 0u);
         }
-        chunk_mma<WT, NT>(acc[cc & 1], va, vb, sa, sb, xf);
+        chunk_mma<WT, NT>(acc[(2 * cc) % NC], acc[(2 * cc + 1) % NC], va, vb, sa, sb, xf);
       }
       __syncwarp();  // every lane's reads of the stage are complete
       if (lane == 0) mbar_arrive(&empty[s]);
-      const int rs = i % RS;
-      if (!mbar_wait(&rfree[rs], ((i / RS) & 1) ^ 1)) {
+      if (!mbar_wait(&rfree[rs], rph ^ 1)) {
         record_error(a.err, ERR_WAIT_RFREE);
         break;
       }
       float* dst = red + ((size_t)(rs * W + cw) * 32 + lane) * NT * 4;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float4*>(dst + nt * 4) =
-            make_float4(acc[0][nt][0] + acc[1][nt][0], acc[0][nt][1] + acc[1][nt][1],
-                        acc[0][nt][2] + acc[1][nt][2], acc[0][nt][3] + acc[1][nt][3]);
+      for (int nt = 0; nt < NT; ++nt) {
+        float o[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          o[r] = NC == 4 ? (acc[0][nt][r] + acc[1][nt][r]) + (acc[2 % NC][nt][r] + acc[3 % NC][nt][r])
+                         : acc[0][nt][r] + acc[1][nt][r];
+        *reinterpret_cast<float4*>(dst + nt * 4) = make_float4(o[0], o[1], o[2], o[3]);
+      }
       if (scale_lane) {
         sred[rs * 64 + rt * 16 + pg] = r0;
         sred[rs * 64 + rt * 16 + pg8] = r1;
       }
       __syncwarp();  // orders the lanes' stores before the release
       if (lane == 0) mbar_arrive(&rfull[rs]);
+      if (++rs == RS) {
+        rs = 0;
+        rph ^= 1;
+      }
     }
   } else {
     // ---------------------------------------------------------------- epilogue warps
@@ -269,11 +288,12 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) best[nt][0] = best[nt][1] = 0ull;
     const bool do_argmax = a.am_keys != nullptr;
-    for (int i = e; i < my_units; i += E) {
-      const int u = first + i * stride;
-      const int tg = u / ksplit, ks = u - tg * ksplit;
+    UnitCursor cu;  // units e, e + E, ... of this CTA; slot e, parity flipping per unit
+    cu.init(first + e * stride, E * stride, ksplit, 1);
+    for (int i = e; i < my_units; i += E, cu.next()) {
+      const int tg = cu.q, ks = cu.r;
       const int rs = e;
-      if (!mbar_wait(&rfull[rs], (i / RS) & 1)) {
+      if (!mbar_wait(&rfull[rs], cu.ph)) {
         record_error(a.err, ERR_WAIT_RED);
         break;
       }
@@ -395,14 +415,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
                     argmax_key((uint32_t)__bfloat16_as_ushort(o), (uint32_t)(a.row_offset + n));
                 key = k > key ? k : key;
               }
-              if (do_argmax) {
-#pragma unroll
-                for (int o = 4; o < 32; o <<= 1) {
-                  const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-                  key = other > key ? other : key;
-                }
-                if (key > best[nt][p]) best[nt][p] = key;
-              }
+              if (key > best[nt][p]) best[nt][p] = key;  // lanes of one token: reduced at the end
             }
           }
         }
@@ -410,6 +423,16 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
     }
 
     if (do_argmax) {
+      // the eight lanes (g = 0..7) that share a token column hold its per-lane maxima
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best[nt][p], o);
+            best[nt][p] = other > best[nt][p] ? other : best[nt][p];
+          }
       if (g == 0) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)

@@ -88,7 +88,8 @@ struct DensePlan {
   size_t smem;
 };
 
-int finish_plan(int M, int K, int NT, DensePlan& p) {
+// Fill in the derived fields and the ring depth; false when two stages do not fit.
+bool layout_plan(int M, int K, int NT, DensePlan& p) {
   p.E = 2;
   p.UB = p.nch_u * 64;
   p.TILE = fnx::tile_bytes(p.UB);
@@ -96,11 +97,16 @@ int finish_plan(int M, int K, int NT, DensePlan& p) {
   p.n_units = p.tile_groups * p.ksplit;
   const int stage = fnx::dense_stage(p.wt == FNX_W_NVFP4, p.RT, p.TILE, p.nch_u).bytes;
   const fnx::DenseLayout L0 = fnx::dense_layout(M, K, p.W, 0, p.E, NT, stage);
-  if ((size_t)L0.total + 2 * (size_t)stage + 256 > kMaxSmem)
-    return fail(FNX_EUNSUPPORTED, "shared memory: M=%d K=%d leaves no room for 2 stages", M, K);
+  if ((size_t)L0.total + 2 * (size_t)stage + 256 > kMaxSmem) return false;
   const int ns = (int)((kMaxSmem - L0.total - 256) / stage);
   p.NS = std::max(2, std::min(ns, 8));
   p.smem = fnx::dense_layout(M, K, p.W, p.NS, p.E, NT, stage).total;
+  return true;
+}
+
+int finish_plan(int M, int K, int NT, DensePlan& p) {
+  if (!layout_plan(M, K, NT, p))
+    return fail(FNX_EUNSUPPORTED, "shared memory: M=%d K=%d leaves no room for 2 stages", M, K);
   return FNX_OK;
 }
 
@@ -178,22 +184,49 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
     return finish_plan(M, K, NT, p);
   }
   const int sms = fnx::num_sms();
-  // Smallest k split whose unit tiles onto the consumer warps and that gives every SM
-  // two units; without such a split, the largest split that tiles.
-  int best = -1;
+  // Search (k split, row tiles per unit RT, chunks per consumer warp CPW) with a cost
+  // model of one CTA's time: rounds of units x the unit's chunk rows, plus a per-unit
+  // overhead of each consumer warp (about 1.5 chunks) and of the split-K fix-up; fewer
+  // than 12 consumer warps hide latency less well.  Measured on lm_head (151936 x 2048
+  // int8, M = 1): 16 warps x 4 chunks x 2 tiles runs at 96 % of the copy bandwidth,
+  // 16 x 2 x 1 at 80 %.
+  double best_cost = 1e30;
+  DensePlan best = p;
+  bool found = false;
   for (int k = 1; k <= nch; ++k) {
     if (nch % k) continue;
-    int w, cpw, rt;
-    if (!tile_unit(nch / k, w, cpw, rt)) continue;
-    best = k;
-    if ((int64_t)p.row_tiles * k >= sms) break;
-    if (nch / k <= 4) break;  // keep at least 4 chunks (256 B of each row) per unit
+    const int nu = nch / k;
+    for (int rt : {1, 2, 4}) {
+      for (int cpw : {1, 2, 4, 8}) {
+        if (nu % cpw) continue;
+        const int ksl = nu / cpw, w = rt * ksl;
+        if (w < 4 || w > 16) continue;
+        DensePlan q = p;
+        q.ksplit = k;
+        q.nch_u = nu;
+        q.W = w;
+        q.CPW = cpw;
+        q.RT = rt;
+        if (!layout_plan(M, K, NT, q)) continue;
+        // several tiles per unit only while every SM still gets two units or more:
+        // small problems are latency-bound and want the most parallel units
+        if (rt > 1 && (int64_t)q.tile_groups * k < 2LL * sms) continue;
+        const int64_t units = q.n_units;
+        const int64_t grid = std::min<int64_t>(units, sms);
+        const int64_t rounds = (units + grid - 1) / grid;
+        double cost = (double)rounds * rt * (nu + 1.5 * ksl + (k > 1 ? 2.0 : 0.0));
+        if (w < 12) cost *= 1.25;
+        if (cost < best_cost - 1e-9) {
+          best_cost = cost;
+          best = q;
+          found = true;
+        }
+      }
+    }
   }
-  if (best < 0) return fail(FNX_EUNSUPPORTED, "no tiling of K=%d (%d chunks)", K, nch);
-  p.ksplit = best;
-  p.nch_u = nch / best;
-  tile_unit(p.nch_u, p.W, p.CPW, p.RT);
-  return finish_plan(M, K, NT, p);
+  if (!found) return fail(FNX_EUNSUPPORTED, "no tiling of K=%d (%d chunks) fits M=%d", K, nch, M);
+  p = best;
+  return FNX_OK;
 }
 
 struct DenseCall {

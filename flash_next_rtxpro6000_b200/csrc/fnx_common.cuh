@@ -194,9 +194,12 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
 // chunk holds k0 .. k0+7 of MMAs 2q and 2q+1.
 // ------------------------------------------------------------------------------------
 template <int WT, int NT>
-__device__ __forceinline__ void chunk_mma(float (&acc)[NT][4], const uint4& va, const uint4& vb,
-                                          uint32_t sa, uint32_t sb,
-                                          const uint4 (&xf)[NT][Geo<WT>::Q], int nt_act = NT) {
+__device__ __forceinline__ void chunk_mma(float (&acc0)[NT][4], float (&acc1)[NT][4],
+                                          const uint4& va, const uint4& vb, uint32_t sa,
+                                          uint32_t sb, const uint4 (&xf)[NT][Geo<WT>::Q],
+                                          int nt_act = NT) {
+  // MMAs alternate between two accumulator sets (even / odd j) so that consecutive
+  // tensor-core instructions do not wait on each other's results.
   const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
   const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
   if constexpr (WT == W_INT8 || WT == W_FP8) {
@@ -216,7 +219,7 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[NT][4], const uint4& va, 
         const uint4& u = xf[nt][j >> 1];
         const uint32_t b0 = (j & 1) ? u.z : u.x;
         const uint32_t b1 = (j & 1) ? u.w : u.y;
-        mma_f16(acc[nt], a0, a1, a2, a3, b0, b1);
+        mma_f16((j & 1) ? acc1[nt] : acc0[nt], a0, a1, a2, a3, b0, b1);
       }
     }
   } else if constexpr (WT == W_BF16) {
@@ -230,7 +233,7 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[NT][4], const uint4& va, 
         const uint4& u = xf[nt][0];
         const uint32_t b0 = j ? u.z : u.x;
         const uint32_t b1 = j ? u.w : u.y;
-        mma_bf16(acc[nt], a0, a1, a2, a3, b0, b1);
+        mma_bf16(j ? acc1[nt] : acc0[nt], a0, a1, a2, a3, b0, b1);
       }
     }
   } else {  // W_NVFP4
@@ -258,7 +261,7 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[NT][4], const uint4& va, 
           const uint4& u = xf[nt][j >> 1];
           const uint32_t b0 = (j & 1) ? u.z : u.x;
           const uint32_t b1 = (j & 1) ? u.w : u.y;
-          mma_f16(acc[nt], a0, a1, a2, a3, b0, b1);
+          mma_f16(h ? acc1[nt] : acc0[nt], a0, a1, a2, a3, b0, b1);
         }
       }
     }
@@ -369,42 +372,77 @@ __device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
 
 // Stage `nrows` activation rows of K bf16 into shared memory in the fragment order above.
 // Row r is read from src(r) (a bf16 pointer, or nullptr for a row that is never used).
-// Each warp takes one row: pass 1 finds max |x|, pass 2 converts with the row's power of
-// two (fp16) or copies it unchanged (bf16 weights, `keep_bf16`).  unscale[r] receives
-// the inverse power of two that the epilogue applies.  Reads use ld.global.cg: the rows
-// may have been written by the previous kernel of a programmatic-dependent pair.
+// Pass 1 finds each row's max |x|, pass 2 converts with the row's power of two (fp16),
+// or the rows are copied unchanged (bf16 weights).  unscale[r] receives the inverse
+// power of two that the epilogue applies.  Reads use ld.global.cg: the rows may have
+// been written by the previous kernel of a programmatic-dependent pair.  Callers
+// synchronise the CTA after the call.
 template <int WT, typename SrcFn>
 __device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int K,
                                            SrcFn src) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  // All threads of the CTA take part (each 16-byte unit of the nrows x K block is one
+  // work item), so the loads of a row are in flight together instead of one warp
+  // walking the row.  unscale[] has room for 2 x 16 words: [16, 32) collects the row
+  // maxima as float bits (non-negative floats order like their bits).
+  const int tid = threadIdx.x, lane = tid & 31, nth = blockDim.x;
   const int srow = stage_row_bytes(K);
   const int units = K >> 3;
-  for (int r = warp; r < nrows; r += nwarps) {
-    const __nv_bfloat16* p = src(r);
-    if (p == nullptr) {
-      if (lane == 0) unscale[r] = 0.f;
-      continue;
+  const int total = nrows * units;
+  if constexpr (WT == W_BF16) {
+    for (int idx = tid; idx < total; idx += nth) {
+      const int r = idx / units, u = idx - r * units;
+      const __nv_bfloat16* p = src(r);
+      const uint4 v = p ? ldg_cg_u4(p + 8 * u) : make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) = v;
     }
-    uint8_t* dst = xs + (size_t)r * srow;
-    if constexpr (WT == W_BF16) {
-      for (int u = lane; u < units; u += 32) {
-        const uint4 v = ldg_cg_u4(p + 8 * u);
-        *reinterpret_cast<uint4*>(dst + stage_unit_offset<WT>(8 * u)) = v;
-      }
-      if (lane == 0) unscale[r] = 1.f;
-    } else {
-      float m = 0.f;
-      for (int u = lane; u < units; u += 32) m = fmaxf(m, bf16x8_absmax(ldg_cg_u4(p + 8 * u)));
+    for (int r = tid; r < nrows; r += nth) unscale[r] = src(r) ? 1.f : 0.f;
+    return;
+  } else {
+    unsigned* smax = reinterpret_cast<unsigned*>(unscale + 16);
+    for (int r = tid; r < nrows; r += nth) smax[r] = 0u;
+    __syncthreads();
+    constexpr int kHold = 4;  // units kept in registers between the two passes
+    const int wbase = tid - lane;  // first work item of this warp (warp-uniform loops)
+    uint4 held[kHold];
+    auto load = [&](int idx) -> uint4 {
+      if (idx >= total) return make_uint4(0u, 0u, 0u, 0u);
+      const int r = idx / units;
+      const __nv_bfloat16* p = src(r);
+      return p ? ldg_cg_u4(p + 8 * (idx - r * units)) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    // Row maximum of one unit per lane: one atomic per warp when the warp's units all
+    // lie in one row, else one per lane.
+    auto row_max = [&](int idx, const uint4 v) {
+      const int r = idx < total ? idx / units : -1;
+      unsigned bits = __float_as_uint(bf16x8_absmax(v));
+      const int r0 = __shfl_sync(0xffffffffu, r, 0);
+      if (__all_sync(0xffffffffu, r == r0)) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const int e = stage_exponent(m);
-      for (int u = lane; u < units; u += 32) {
-        const uint4 v = ldg_cg_u4(p + 8 * u);
-        *reinterpret_cast<uint4*>(dst + stage_unit_offset<WT>(8 * u)) =
-            bf16x8_to_f16x8_scaled(v, e);
+        for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+        if (lane == 0 && r0 >= 0) atomicMax(&smax[r0], bits);
+      } else if (r >= 0) {
+        atomicMax(&smax[r], bits);
       }
-      if (lane == 0) unscale[r] = pow2f(-e);
-    }
+    };
+#pragma unroll
+    for (int j = 0; j < kHold; ++j) held[j] = load(tid + j * nth);
+#pragma unroll
+    for (int j = 0; j < kHold; ++j)
+      if (wbase + j * nth < total) row_max(tid + j * nth, held[j]);
+    for (int b = wbase + kHold * nth; b < total; b += nth) row_max(b + lane, load(b + lane));
+    __syncthreads();
+    auto put = [&](int idx, const uint4 v) {
+      if (idx >= total) return;
+      const int r = idx / units, u = idx - r * units;
+      const int e = stage_exponent(__uint_as_float(smax[r]));
+      *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) =
+          bf16x8_to_f16x8_scaled(v, e);
+    };
+#pragma unroll
+    for (int j = 0; j < kHold; ++j) put(tid + j * nth, held[j]);
+    for (int idx = tid + kHold * nth; idx < total; idx += nth) put(idx, load(idx));
+    for (int r = tid; r < nrows; r += nth)
+      unscale[r] = src(r) ? pow2f(-stage_exponent(__uint_as_float(smax[r]))) : 0.f;
   }
 }
 
@@ -454,6 +492,22 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_test, but a thread whose phase has not completed is suspended (it issues no
+// instructions) until the phase completes or about `suspend_ns` nanoseconds pass, so
+// waiting warps leave the issue slots to the warps that have work.
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity,
+                                                  uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -465,9 +519,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (mbar_test(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity, 1000000u)) return true;
     if (global_ns() - t0 > kWaitLimitNs) return false;
   }
 }
@@ -522,6 +574,39 @@ __host__ __device__ constexpr int tile_half_offset(int ub) {
 __host__ __device__ constexpr int tile_bytes(int ub) {
   return ((tile_half_offset(ub) + 8 * ub) + 127) / 128 * 128;
 }
+// A persistent CTA's units are u0, u0 + step, ...  UnitCursor walks them, with
+// u / div and u % div and the ring stage (ordinal % ns) and its phase parity
+// ((ordinal / ns) & 1), without a division per unit.
+struct UnitCursor {
+  int u, q, r, s, ph;
+  int dq, dr, div, ns, step;
+  __device__ __forceinline__ void init(int u0, int step_, int div_, int ns_) {
+    step = step_;
+    div = div_;
+    ns = ns_;
+    u = u0;
+    q = u0 / div_;
+    r = u0 - q * div_;
+    dq = step_ / div_;
+    dr = step_ - dq * div_;
+    s = 0;
+    ph = 0;
+  }
+  __device__ __forceinline__ void next() {
+    u += step;
+    q += dq;
+    r += dr;
+    if (r >= div) {
+      r -= div;
+      ++q;
+    }
+    if (++s == ns) {
+      s = 0;
+      ph ^= 1;
+    }
+  }
+};
+
 // Physical row of MMA row g (0..7) and of MMA row g + 8, for the lane's g.
 __device__ __forceinline__ int phys_lo(int g) { return (g & 1) ? g + 8 : g; }
 __device__ __forceinline__ int phys_hi(int g) { return (g & 1) ? g : g + 8; }

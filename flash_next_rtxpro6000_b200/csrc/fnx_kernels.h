@@ -84,7 +84,7 @@ __host__ __device__ inline DenseLayout dense_layout(int M, int K, int W, int NS,
   L.xs = dense_align(off, 128);
   off = L.xs + M * (2 * K + 64);
   L.unscale = dense_align(off, 16);
-  off = L.unscale + 16 * 4;
+  off = L.unscale + 32 * 4;  // 16 unscale factors + 16 row maxima (stage_rows)
   L.red = dense_align(off, 16);
   off = L.red + RS * W * 32 * NT * 16;
   L.sred = off;                       // per slot: 64 floats of row scales (RT x 16)
@@ -168,7 +168,7 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   L.xs = off;
   off += kernel == 1 ? M * (2 * H + 64) : 0;
   L.unscale = dense_align(off, 16);
-  off = L.unscale + 16 * 4;
+  off = L.unscale + 32 * 4;  // 16 unscale factors + 16 row maxima (stage_rows)
   L.red = dense_align(off, 16);
   off = L.red + RS * W * 32 * NT * 16 + RS * 64 * 4;  // partial tiles, then 64 floats/slot
   L.ids = off;

@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeAr
             xf[nt][q] = tok[nt] >= 0
                             ? lds128(xs + (size_t)tok[nt] * srow + ((ch * Q + q) * 4 + c) * 16)
                             : make_uint4(0u, 0u, 0u, 0u);
-        chunk_mma<W_NVFP4, NT>(acc[cc & 1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
+        chunk_mma<W_NVFP4, NT>(acc[0], acc[1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -606,7 +606,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_down_kernel(const Moe
             xf[nt][q] = sl < ur.n ? lds128(bst + (size_t)sl * L.bpitch + ((ch * Q + q) * 4 + c) * 16)
                                   : make_uint4(0u, 0u, 0u, 0u);
         }
-        chunk_mma<W_NVFP4, NT>(acc[cc & 1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
+        chunk_mma<W_NVFP4, NT>(acc[0], acc[1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
