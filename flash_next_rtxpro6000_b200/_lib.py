@@ -76,11 +76,7 @@ class FnxMoeWeights(ctypes.Structure):
 class FnxMoeWorkspace(ctypes.Structure):
     _fields_ = [
         ("act", c_void_p),
-        ("act_f16", c_void_p),
-        ("pair_unscale", c_void_p),
-        ("expert_counters", c_void_p),
         ("partials", c_void_p),
-        ("counters", c_void_p),
         ("error_flag", c_void_p),
         ("max_m", c_int),
         ("max_routes", c_int),
@@ -90,11 +86,7 @@ class FnxMoeWorkspace(ctypes.Structure):
 class FnxMoeWorkspaceSizes(ctypes.Structure):
     _fields_ = [
         ("act", c_int64),
-        ("act_f16", c_int64),
-        ("pair_unscale", c_int64),
-        ("expert_counters", c_int64),
         ("partials", c_int64),
-        ("counters", c_int64),
     ]
 
 

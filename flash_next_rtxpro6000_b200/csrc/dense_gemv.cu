@@ -160,10 +160,13 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
   }
   // The weights and scales do not depend on the previous kernel; the activations may.
   pdl_wait();
-  stage_rows<WT>(xs, unscale, M, K, [&](int r) {
-    return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
-  });
-  __syncthreads();
+  // The other warps stage the activations meanwhile; the producer never waits for them.
+  if (warp > 0) {
+    stage_rows<WT>(xs, unscale, M, K, [&](int r) {
+      return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
+    }, 32, blockDim.x - 32, 1);
+    group_sync(1, blockDim.x - 32);
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer

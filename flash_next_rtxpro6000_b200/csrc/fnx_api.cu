@@ -110,55 +110,6 @@ int finish_plan(int M, int K, int NT, DensePlan& p) {
   return FNX_OK;
 }
 
-// Consumer warps W (any count up to 16), chunks per warp CPW and row tiles per unit RT
-// for a unit of `nch_u` 64-byte chunks per row: prefer 8..16 warps, each streaming one
-// to eight chunks; a short unit takes several row tiles so 8 warps still have work.
-bool tile_unit(int nch_u, int& W, int& CPW, int& RT) {
-  for (int lo : {8, 4}) {
-    for (int cpw : {1, 2, 4, 8}) {
-      if (nch_u % cpw) continue;
-      const int w = nch_u / cpw;
-      if (w >= lo && w <= 16) {
-        W = w;
-        CPW = cpw;
-        RT = 1;
-        return true;
-      }
-    }
-  }
-  if (nch_u < 8 && 8 % nch_u == 0) {
-    RT = std::min(4, 8 / nch_u);
-    W = RT * nch_u;
-    CPW = 1;
-    return true;
-  }
-  for (int cpw : {1, 2, 4, 8}) {
-    if (nch_u % cpw == 0 && nch_u / cpw <= 16) {
-      W = nch_u / cpw;
-      CPW = cpw;
-      RT = 1;
-      return true;
-    }
-  }
-  return false;
-}
-
-// k2 (down projection) tiling: the most 16-row tiles per unit (up to 4) whose
-// RT x (I / 128 / CPW) consumer warps fit in 16 and whose rows divide H.
-bool down_tiling(int H, int I, int& CPW, int& RT) {
-  const int ch2 = I / 128;
-  for (int rt = 4; rt >= 1; --rt) {
-    if (H % (16 * rt)) continue;
-    for (int c : {1, 2, 4})
-      if (ch2 % c == 0 && rt * (ch2 / c) <= 16) {
-        CPW = c;
-        RT = rt;
-        return true;
-      }
-  }
-  return false;
-}
-
 int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, DensePlan& p) {
   const int CH = chunk_k(wt);
   if (K <= 0 || K % CH)
@@ -200,7 +151,7 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
       for (int cpw : {1, 2, 4, 8}) {
         if (nu % cpw) continue;
         const int ksl = nu / cpw, w = rt * ksl;
-        if (w < 4 || w > 16) continue;
+        if (w > 16) continue;
         DensePlan q = p;
         q.ksplit = k;
         q.nch_u = nu;
@@ -216,6 +167,7 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
         const int64_t rounds = (units + grid - 1) / grid;
         double cost = (double)rounds * rt * (nu + 1.5 * ksl + (k > 1 ? 2.0 : 0.0));
         if (w < 12) cost *= 1.25;
+        if (w < 4) cost *= 2.0;
         if (cost < best_cost - 1e-9) {
           best_cost = cost;
           best = q;
@@ -363,33 +315,44 @@ int run_dense(const DenseCall& c) {
 
 // Launch geometry of the two MoE kernels for M tokens x R routes over E experts.
 struct MoeGeo {
-  int NT, w1, cpw1, ns1, w2, cpw2, rt2, ns2;
+  int NT, w1, cpw1, ns1, cpw2, ns2, EW;
   size_t smem1, smem2;
 };
+
+// k1 (gate/up) tiling: H / 128 chunks per row split over W consumer warps of CPW chunks;
+// two chunks per warp preferred (fewer per-unit hand-overs), 4 to 16 warps.
+bool up_tiling(int H, int& W, int& CPW) {
+  const int ch1 = H / 128;
+  for (int c : {2, 1, 4})
+    if (ch1 % c == 0 && ch1 / c >= 4 && ch1 / c <= 16) {
+      CPW = c;
+      W = ch1 / c;
+      return true;
+    }
+  return false;
+}
 
 int moe_geometry(int M, int R, int E, int H, int I, MoeGeo& g) {
   if (H % 128 || I % 128 || H <= 0 || I <= 0)
     return fail(FNX_EUNSUPPORTED, "H=%d and I=%d must be multiples of 128", H, I);
   g.NT = M > 8 ? 2 : 1;
-  // k1: consumers split H (chunks of 128) into W slices of CPW chunks.
-  int rt1 = 0;
-  if (!tile_unit(H / 128, g.w1, g.cpw1, rt1) || rt1 != 1 || g.cpw1 > 4)
-    return fail(FNX_EUNSUPPORTED, "H=%d: no gate/up tiling", H);
-  // k2: units of RT 16-row tiles; consumers = RT tiles x (I / 128 / CPW) k slices.
-  if (!down_tiling(H, I, g.cpw2, g.rt2)) return fail(FNX_EUNSUPPORTED, "I=%d: no down tiling", I);
-  g.w2 = g.rt2 * (I / 128 / g.cpw2);
-  const int RS = 2;
-  auto stages_for = [&](int kernel, int W, int RT) {
-    const fnx::MoeLayout L0 = fnx::moe_layout(kernel, M, R, E, H, I, W, 0, RS, g.NT, RT);
-    const int64_t ns = ((int64_t)kMaxSmem - L0.total - 256) / L0.stage_bytes;
+  g.EW = 2;
+  if (!up_tiling(H, g.w1, g.cpw1)) return fail(FNX_EUNSUPPORTED, "H=%d: no gate/up tiling", H);
+  // k2: each consumer warp streams one 16-row tile over all of I (I / 128 chunks)
+  g.cpw2 = I / 128;
+  if (g.cpw2 != 1 && g.cpw2 != 2 && g.cpw2 != 4 && g.cpw2 != 5 && g.cpw2 != 8)
+    return fail(FNX_EUNSUPPORTED, "I=%d: the down kernel takes I in {128, 256, 512, 640, 1024}", I);
+  auto stages_for = [&](int kernel, int W, int RS, int nbar) {
+    const fnx::MoeLayout L0 = fnx::moe_layout(kernel, M, R, E, H, I, W, 0, RS, g.NT, 8);
+    const int64_t ns = ((int64_t)kMaxSmem - L0.total - 256) / (L0.stage_bytes + 8 * nbar);
     return (int)std::min<int64_t>(ns, 8);
   };
-  g.ns1 = stages_for(1, g.w1, 1);
-  g.ns2 = stages_for(2, g.w2, g.rt2);
+  g.ns1 = stages_for(1, g.w1, g.EW, 2);
+  g.ns2 = stages_for(2, 8, 0, 3);
   if (g.ns1 < 2 || g.ns2 < 2)
     return fail(FNX_EUNSUPPORTED, "MoE shared memory too small for M=%d, H=%d, I=%d", M, H, I);
-  g.smem1 = fnx::moe_layout(1, M, R, E, H, I, g.w1, g.ns1, RS, g.NT, 1).total;
-  g.smem2 = fnx::moe_layout(2, M, R, E, H, I, g.w2, g.ns2, RS, g.NT, g.rt2).total;
+  g.smem1 = fnx::moe_layout(1, M, R, E, H, I, g.w1, g.ns1, g.EW, g.NT, 8).total;
+  g.smem2 = fnx::moe_layout(2, M, R, E, H, I, 8, g.ns2, 0, g.NT, 8).total;
   return FNX_OK;
 }
 
@@ -549,12 +512,8 @@ int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, i
   if (int rc = moe_geometry(max_m, max_routes, num_experts, H, I, geo)) return rc;
   const int64_t pairs = (int64_t)max_m * (max_routes + 1);
   const int64_t dcap = std::min<int64_t>(num_experts, (int64_t)max_m * max_routes) + 1;
-  out->act = pairs * I * 2;
-  out->act_f16 = dcap * 16 * (2LL * I + 64);
-  out->pair_unscale = dcap * 16 * 4;
-  out->expert_counters = dcap * 4;
+  out->act = dcap * 16 * (2LL * I + 64);
   out->partials = pairs * H * 4;
-  out->counters = (int64_t)(H / 16) * 4;  // one per k2 row group (16 * RT rows, RT >= 1)
   return FNX_OK;
 }
 
@@ -588,11 +547,9 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
     if (!aligned(shared->w13, 16) || !aligned(shared->w2, 16))
       return fail(FNX_EINVAL, "shared expert weights must be 16-byte aligned");
   }
-  if (!ws->act || !ws->act_f16 || !ws->pair_unscale || !ws->expert_counters || !ws->partials ||
-      !ws->counters || ws->max_m < M || ws->max_routes < R)
+  if (!ws->act || !ws->partials || ws->max_m < M || ws->max_routes < R)
     return fail(FNX_EINVAL, "MoE workspace missing or sized for fewer tokens/routes");
-  if (!aligned(ws->act_f16, 16) || !aligned(ws->act, 16))
-    return fail(FNX_EINVAL, "MoE workspace act buffers must be 16-byte aligned");
+  if (!aligned(ws->act, 16)) return fail(FNX_EINVAL, "MoE workspace act rows must be 16-byte aligned");
   // The routes of one token address act rows t * (R + 1) + r of the workspace's
   // (max_routes + 1)-wide layout only when R == max_routes; use the call's R instead.
   const int NT = M > 8 ? 2 : 1;
@@ -629,31 +586,28 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   a.has_shared = has_shared;
   a.swizzled = experts->scales_swizzled;
   a.e_lo = experts->expert_offset;
-  a.act = ws->act;
-  a.act_f16 = static_cast<uint8_t*>(ws->act_f16);
-  a.pair_unscale = ws->pair_unscale;
-  a.ecnt = ws->expert_counters;
+  a.act = static_cast<uint8_t*>(ws->act);
   a.part = ws->partials;
-  a.cnt = ws->counters;
   a.err = ws->error_flag;
   a.out = out;
   a.ldo = ldo;
   a.out_f32 = out_f32;
-  a.RS = 2;
   a.NT = NT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   MoeGeo geo;
   if (int rc = moe_geometry(M, R, E, H, I, geo)) return rc;
   const int w1 = geo.w1, cpw1 = geo.cpw1, ns1 = geo.ns1;
-  const int w2 = geo.w2, cpw2 = geo.cpw2, rt2 = geo.rt2, ns2 = geo.ns2;
+  const int cpw2 = geo.cpw2, ns2 = geo.ns2;
+  a.EW = geo.EW;
+  a.RS = geo.EW;
 
   a.W = w1;
   a.CPW = cpw1;
   a.NS = ns1;
   a.pdl = pdl;
   const size_t smem1 = geo.smem1;
-  const int occ1 = fnx::moe_up_occupancy(NT, cpw1, (w1 + 2) * 32, smem1);
+  const int occ1 = fnx::moe_up_occupancy(NT, cpw1, (w1 + 1 + a.EW) * 32, smem1);
   if (occ1 <= 0) return fail(FNX_EUNSUPPORTED, "k1 does not fit on an SM");
   const int64_t units1 = (int64_t)dmax * (I / 8);
   const int grid1 = (int)std::min<int64_t>(units1, (int64_t)sms * occ1);
@@ -661,19 +615,20 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no k1 instance");
   if (rc) return cuda_fail("MoE k1 launch");
 
-  a.W = w2;
+  a.W = 8;
   a.CPW = cpw2;
-  a.RT = rt2;
   a.NS = ns2;
-  a.pdl = 1;  // k2 streams W2 while k1 drains
+  a.RS = 0;
+  a.pdl = 1;  // k2 decodes the routes and streams W2 while k1 drains
   const size_t smem2 = geo.smem2;
-  const int occ2 = fnx::moe_down_occupancy(NT, cpw2, (w2 + 2) * 32, smem2);
+  const int occ2 = fnx::moe_down_occupancy(NT, cpw2, 10 * 32, smem2);
   if (occ2 <= 0) return fail(FNX_EUNSUPPORTED, "k2 does not fit on an SM");
-  const int64_t units2 = (int64_t)dmax * (H / (16 * rt2));
+  const int64_t units2 = (int64_t)dmax * (H / 128);
   const int grid2 = (int)std::min<int64_t>(units2, (int64_t)sms * occ2);
   rc = fnx::launch_moe_down(a, NT, grid2, smem2, st);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no k2 instance");
   if (rc) return cuda_fail("MoE k2 launch");
+  if (fnx::launch_moe_sum(a, st)) return cuda_fail("MoE route-sum launch");
   return FNX_OK;
 }
 

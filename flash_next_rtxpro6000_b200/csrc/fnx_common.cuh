@@ -376,15 +376,15 @@ __device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
 // or the rows are copied unchanged (bf16 weights).  unscale[r] receives the inverse
 // power of two that the epilogue applies.  Reads use ld.global.cg: the rows may have
 // been written by the previous kernel of a programmatic-dependent pair.  Callers
-// synchronise the CTA after the call.
+// synchronise the participating threads (named barrier bar_id) after the call.
 template <int WT, typename SrcFn>
 __device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int K,
-                                           SrcFn src) {
-  // All threads of the CTA take part (each 16-byte unit of the nrows x K block is one
-  // work item), so the loads of a row are in flight together instead of one warp
-  // walking the row.  unscale[] has room for 2 x 16 words: [16, 32) collects the row
-  // maxima as float bits (non-negative floats order like their bits).
-  const int tid = threadIdx.x, lane = tid & 31, nth = blockDim.x;
+                                           SrcFn src, int t0, int nth, int bar_id) {
+  // Threads t0 .. t0 + nth - 1 (whole warps) take part and synchronise on named barrier
+  // bar_id; each 16-byte unit of the nrows x K block is one work item, so the loads of a
+  // row are in flight together.  unscale[] has room for 2 x 16 words: [16, 32) collects
+  // the row maxima as float bits (non-negative floats order like their bits).
+  const int tid = threadIdx.x - t0, lane = threadIdx.x & 31;
   const int srow = stage_row_bytes(K);
   const int units = K >> 3;
   const int total = nrows * units;
@@ -400,7 +400,7 @@ __device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrow
   } else {
     unsigned* smax = reinterpret_cast<unsigned*>(unscale + 16);
     for (int r = tid; r < nrows; r += nth) smax[r] = 0u;
-    __syncthreads();
+    group_sync(bar_id, nth);
     constexpr int kHold = 4;  // units kept in registers between the two passes
     const int wbase = tid - lane;  // first work item of this warp (warp-uniform loops)
     uint4 held[kHold];
@@ -429,8 +429,15 @@ __device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrow
 #pragma unroll
     for (int j = 0; j < kHold; ++j)
       if (wbase + j * nth < total) row_max(tid + j * nth, held[j]);
-    for (int b = wbase + kHold * nth; b < total; b += nth) row_max(b + lane, load(b + lane));
-    __syncthreads();
+    for (int b = wbase + kHold * nth; b < total; b += kHold * nth) {  // batches of kHold
+      uint4 v[kHold];
+#pragma unroll
+      for (int j = 0; j < kHold; ++j) v[j] = load(b + lane + j * nth);
+#pragma unroll
+      for (int j = 0; j < kHold; ++j)
+        if (b + j * nth < total) row_max(b + lane + j * nth, v[j]);
+    }
+    group_sync(bar_id, nth);
     auto put = [&](int idx, const uint4 v) {
       if (idx >= total) return;
       const int r = idx / units, u = idx - r * units;
@@ -440,7 +447,13 @@ __device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrow
     };
 #pragma unroll
     for (int j = 0; j < kHold; ++j) put(tid + j * nth, held[j]);
-    for (int idx = tid + kHold * nth; idx < total; idx += nth) put(idx, load(idx));
+    for (int b = tid + kHold * nth; b < total; b += kHold * nth) {
+      uint4 v[kHold];
+#pragma unroll
+      for (int j = 0; j < kHold; ++j) v[j] = load(b + j * nth);
+#pragma unroll
+      for (int j = 0; j < kHold; ++j) put(b + j * nth, v[j]);
+    }
     for (int r = tid; r < nrows; r += nth)
       unscale[r] = src(r) ? pow2f(-stage_exponent(__uint_as_float(smax[r]))) : 0.f;
   }
@@ -522,6 +535,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_test_suspend(bar, parity, 1000000u)) return true;
     if (global_ns() - t0 > kWaitLimitNs) return false;
   }
+}
+
+// Generic-proxy writes to shared memory become ordered before later async-proxy (bulk
+// copy) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Atomic add with acquire-release semantics at GPU scope: this thread's earlier writes
+// (and those ordered before them, e.g. by __syncwarp) are visible to whoever observes the
+// new value, and the returned old value carries the writes of earlier releasers.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 // Bulk copy global -> this CTA's shared memory, completing `bytes` on the mbarrier.

@@ -123,27 +123,28 @@ struct MoeArgs {
   // [e_lo, e_lo + E) are skipped; weight tensors hold the local experts only.
   int e_lo;
   // scratch (caller-owned; counters zero between calls)
-  void* act;              // bf16 [M * (R + 1), I]            k1 -> k1 finaliser
-  uint8_t* act_f16;       // [dcap * 16] rows of 2I + 64 B     k1 finaliser -> k2 (B rows),
-                          //   row d * 16 + s = route slot s of distinct expert d
-  float* pair_unscale;    // [dcap * 16]                       inverse power of two per route
-  unsigned int* ecnt;     // [min(E, M*R) + 1]                 k1 units done per expert
-  float* part;            // fp32 [M * (R + 1), H]             k2 route partials
-  unsigned int* cnt;      // [H / 64]                          k2 experts done per row group
+  uint8_t* act;           // [dcap * 16] rows of 2I + 64 B: the SiLU-mul activations in bf16,
+                          //   row d * 16 + s = route slot s of distinct expert d, in the
+                          //   B-operand order of the down kernel (k1 -> k2)
+  float* part;            // fp32 [H / 128][M * (R + 1)][128]  k2 route partials
   int* err;
   // output: bf16 [M, H] (or fp32 partial sums when out_f32, for cross-rank reduction)
   void* out;
   int64_t ldo;
   int out_f32;
-  // launch geometry (RT: 16-row tiles per k2 unit)
-  int W, CPW, NS, RS, NT, RT;
+  // launch geometry (EW: k1 epilogue warps)
+  int W, CPW, NS, RS, NT, EW;
   int pdl;
 };
 
-// Shared-memory layout of the MoE kernels.
+// Shared-memory layout of the MoE kernels.  A stage holds the unit's weight tiles, its
+// e4m3 block scales (row-major, spitch bytes per row), for k2 the B rows of its routes
+// (bpitch bytes each), and a small float area: k1 the expert's global scale; k2 the
+// route weights [0, 16) and the global scale [16], replaced by the route factors.
 struct MoeLayout {
-  int bars, stages, xs, unscale, red, ids, bitmap, wbase, exp_of, cnt_of, ent, misc, total;
-  int stage_bytes, wpitch, bpitch, brow0;  // stage: weight rows then B rows (k2)
+  int bars, stages, xs, unscale, red, sred, ids, bitmap, wbase, exp_of, cnt_of, ent, misc;
+  int ctab, rrank, rdist, etok, epair, total;
+  int stage_bytes, wpitch, soff, spitch, boff, bpitch, foff;
 };
 
 constexpr int kMoeSlotCap = 16;  // routes of one distinct expert handled by one unit
@@ -154,15 +155,24 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   MoeLayout L;
   const int nw = (E + 31) / 32;
   const int dcap = (E < M * R ? E : M * R) + 1;
-  const int ub = (kernel == 1 ? H : I) / 2;
-  L.wpitch = tile_bytes(ub);            // bytes of one 16-row tile
-  const int tiles = kernel == 1 ? 1 : RT;
+  const int K = kernel == 1 ? H : I;
   L.bpitch = 2 * I + 64;
-  L.brow0 = tiles * L.wpitch;
-  L.stage_bytes = dense_align(L.brow0 + (kernel == 2 ? 8 * NT * L.bpitch : 0), 128);
+  if (kernel == 1) {  // one 16-row tile (two 8-row halves), scales of 16 rows
+    L.wpitch = tile_bytes(K / 2);
+    L.spitch = dense_align(K / 16, 16);  // linear scales: one padded row per weight row
+    L.soff = L.wpitch;
+    L.boff = dense_align(L.soff + 16 * L.spitch, 128);  // >= swizzled 16 * K/16
+  } else {            // 128 contiguous rows, then the 128 rows' scales as one block
+    L.wpitch = 16 * (K / 2);
+    L.spitch = K / 16;
+    L.soff = 8 * L.wpitch;
+    L.boff = dense_align(L.soff + 128 * L.spitch, 128);
+  }
+  L.foff = L.boff + (kernel == 2 ? 8 * NT * L.bpitch : 0);
+  L.stage_bytes = dense_align(L.foff + 80, 128);
   int off = 0;
   L.bars = off;
-  off = dense_align(off + (2 * NS + 2 * RS) * 8, 128);
+  off = dense_align(off + (3 * NS + 2 * RS) * 8, 128);  // full, converted, empty; rfull, rfree
   L.stages = off;
   off += NS * L.stage_bytes;
   L.xs = off;
@@ -170,7 +180,9 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   L.unscale = dense_align(off, 16);
   off = L.unscale + 32 * 4;  // 16 unscale factors + 16 row maxima (stage_rows)
   L.red = dense_align(off, 16);
-  off = L.red + RS * W * 32 * NT * 16 + RS * 64 * 4;  // partial tiles, then 64 floats/slot
+  off = L.red + RS * W * 32 * NT * 16;
+  L.sred = off;               // per slot: 64 floats handed to the epilogue
+  off += RS * 64 * 4;
   L.ids = off;
   off += dense_align(M * R, 4) * 4;
   L.bitmap = off;
@@ -185,6 +197,17 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   off += dense_align(dcap * kMoeSlotCap * 2, 16);
   L.misc = off;
   off += 16;
+  const int n = M * R;
+  L.ctab = off;
+  off += dense_align(((n + 31) / 32) * dcap, 16);
+  L.rrank = off;
+  off += dense_align(n, 16);
+  L.rdist = off;
+  off += dense_align(2 * n, 16);
+  L.etok = off;
+  off += dense_align(n, 16);
+  L.epair = off;
+  off += dense_align(2 * (n + M), 16);
   L.total = dense_align(off, 128);
   return L;
 }
@@ -193,6 +216,7 @@ int launch_dense(const DenseArgs& a, int wtype, int nt, int cpw, int grid, size_
                  cudaStream_t stream);
 int launch_moe_up(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream);
 int launch_moe_down(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream);
+int launch_moe_sum(const MoeArgs& a, cudaStream_t stream);
 int launch_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
                          cudaStream_t stream);
 

