@@ -58,14 +58,19 @@ def measured_peak():
         return FALLBACK_HBM, "fallback (6.65 TB/s earlier pool measurement)"
 
 
-def traffic_for(workload: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
-    p = os.path.join(ROOT, "profiles", f"{workload}.traffic.json")
+def traffic_for(profile: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum of one ncu
+    capture, keyed by token count) from the committed summary profiles/<profile>.md,
+    whose line `traffic_bytes_per_launch: {...}` holds them; None when absent."""
+    p = os.path.join(ROOT, "profiles", f"{profile}.md")
     try:
         with open(p) as f:
-            return json.load(f)
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return json.loads(line.split(":", 1)[1])
     except Exception:
         return None
+    return None
 
 
 # ------------------------------------------------------------------ clocks sampler
@@ -333,7 +338,8 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
     traffic = traffic_for(f"dense_gemv_int8_{args.workload}")
     tr = None
     if traffic and world == 1:
-        tr = sum(traffic.get(str(m), 0) for m in Ms) / max(1, len(Ms))
+        got = [traffic[str(m)] for m in Ms if str(m) in traffic]
+        tr = round(sum(got) / len(got)) if got else None
     res = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
