@@ -240,11 +240,13 @@ def _timed(fn, steps, warmup, dev, world, sampler=None):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    # the clock sampler (a subprocess) starts before the barrier, so no rank enters the
+    # timed region while another is still spawning it
+    if sampler:
+        sampler.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    if sampler:
-        sampler.start()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(steps):
