@@ -361,10 +361,11 @@ int moe_geometry(int M, int R, int E, int H, int I, MoeGeo& g) {
 // C ABI directly (cgo, JNI, a ctypes script) owns the weights and activations it
 // passes in, but has no memory pool to carve a scratch buffer from for every shape.
 // For them the scratch lives in one static array per device, laid out as
-//   [0, 128)      argmax keys (16 x u64)        zero between calls
-//   [256, 260)    argmax counter (u32)          zero between calls
+//   [0, 128)      argmax keys (16 x u64)        cleared before each launch
+//   [256, 260)    argmax counter (u32)          cleared before each launch
 //   [512, 516)    device error word (i32)
-//   [4096, ...)   split-K counters, then split-K partial floats (counters zero between calls)
+//   [4096, ...)   split-K counters (the ones a launch uses are cleared before it), then
+//                 split-K partial floats
 static __device__ __align__(256) unsigned char g_static_scratch[FNX_STATIC_SCRATCH_BYTES];
 
 namespace {
@@ -467,6 +468,13 @@ int fnx_w8a16_gemv_static_ws(const void* x, int64_t ldx, const void* w, int64_t 
   ws.n_counters = FNX_STATIC_COUNTERS;
   ws.partials = reinterpret_cast<float*>(b + 4096 + 4 * FNX_STATIC_COUNTERS);
   ws.partial_floats = FNX_STATIC_PARTIAL_FLOATS;
+  // The array keeps whatever the previous call left; a call that ended early (a wait
+  // that gave up) may have left keys or counters set.  Clear what this launch needs at
+  // zero, on the caller's stream, before it runs (a memset allocates nothing).
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(b, 0, 260, st) != cudaSuccess ||
+      (counters > 0 && cudaMemsetAsync(b + 4096, 0, (size_t)counters * 4, st) != cudaSuccess))
+    return cuda_fail("clearing the static scratch");
   DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, y2, ldy2,
                  split_n, out_f32, argmax_out, argmax_key_out, row_offset, M, N, K, 0,
                  cfg, &ws, pdl, static_cast<cudaStream_t>(stream)};

@@ -211,10 +211,10 @@ int fnx_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
  *   FNX_STATIC_COUNTERS counters is rejected with FNX_EUNSUPPORTED.
  * - The first call on a device resolves the array's address (one-time setup with
  *   that device current); make that first call before capturing a stream.
- * - All calls on a device share the array: calls that may run at the same time
- *   (different streams without ordering) race on it.  The argmax keys, the argmax
- *   counter and the split-K counters must be zero when a call starts; they are zero
- *   at load and every completed call leaves them zero.
+ * - All calls on a device share the array, which keeps the previous call's contents:
+ *   calls that may run at the same time (different streams without ordering) race on
+ *   it.  The argmax keys, the argmax counter and the split-K counters must be zero when
+ *   the kernel starts; each call clears them with a memset on its stream first.
  * - A device-side wait that gives up records its code in the array's error word,
  *   which this entry point does not report; fnx_w8a16_gemv with a workspace does.
  */
