@@ -309,20 +309,21 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
         scl[rt][1] = per_row ? sred[rs * 64 + rt * 16 + pg8] : scalar_scale;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
+          // k slices in batches of four independent loads, summed in slice order on two
+          // chains (even / odd slices)
           float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
-          int kq = 0;
-          for (; kq + 1 < KSL; kq += 2) {  // two chains; fixed order
-            const float4 p = *reinterpret_cast<const float4*>(
-                red + ((size_t)(rs * W + rt * KSL + kq) * 32 + lane) * NT * 4 + nt * 4);
-            const float4 q = *reinterpret_cast<const float4*>(
-                red + ((size_t)(rs * W + rt * KSL + kq + 1) * 32 + lane) * NT * 4 + nt * 4);
-            s0.x += p.x; s0.y += p.y; s0.z += p.z; s0.w += p.w;
-            s1.x += q.x; s1.y += q.y; s1.z += q.z; s1.w += q.w;
-          }
-          if (kq < KSL) {
-            const float4 p = *reinterpret_cast<const float4*>(
-                red + ((size_t)(rs * W + rt * KSL + kq) * 32 + lane) * NT * 4 + nt * 4);
-            s0.x += p.x; s0.y += p.y; s0.z += p.z; s0.w += p.w;
+          const float* rbase = red + ((size_t)(rs * W + rt * KSL) * 32 + lane) * NT * 4 + nt * 4;
+          for (int k0 = 0; k0 < KSL; k0 += 4) {
+            float4 pv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              pv[j] = k0 + j < KSL ? *reinterpret_cast<const float4*>(rbase + (size_t)(k0 + j) * 32 * NT * 4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {
+              s0.x += pv[j].x; s0.y += pv[j].y; s0.z += pv[j].z; s0.w += pv[j].w;
+              s1.x += pv[j + 1].x; s1.y += pv[j + 1].y; s1.z += pv[j + 1].z; s1.w += pv[j + 1].w;
+            }
           }
           v[rt][nt][0] = s0.x + s1.x;
           v[rt][nt][1] = s0.y + s1.y;

@@ -88,9 +88,21 @@ struct DensePlan {
   size_t smem;
 };
 
+bool layout_fits(int M, int K, int NT, DensePlan& p);
+
 // Fill in the derived fields and the ring depth; false when two stages do not fit.
 bool layout_plan(int M, int K, int NT, DensePlan& p) {
-  p.E = 2;
+  // three epilogue warps where the threads and shared memory allow (the epilogue shares
+  // the issue slots with up to 16 consumer warps), else two
+  for (int e = 3; e >= 2; --e) {
+    p.E = e;
+    if (p.W + 1 + e > 20) continue;
+    if (layout_fits(M, K, NT, p)) return true;
+  }
+  return false;
+}
+
+bool layout_fits(int M, int K, int NT, DensePlan& p) {
   p.UB = p.nch_u * 64;
   p.TILE = fnx::tile_bytes(p.UB);
   p.tile_groups = (p.row_tiles + p.RT - 1) / p.RT;

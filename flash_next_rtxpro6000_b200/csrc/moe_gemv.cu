@@ -169,14 +169,6 @@ __device__ void route_decode(const MoeArgs& a, const Routing& rt) {
   __syncthreads();
 }
 
-// Byte offset of the two e4m3 scales of (row, kb..kb+1) inside one expert's scale block.
-__device__ __forceinline__ int64_t scale_offset(int swizzled, int row, int kb, int KP) {
-  if (!swizzled) return (int64_t)row * KP + kb;
-  // 128x4 layout: (m/128)*128*KP + (kb/4)*512 + (m%32)*16 + ((m%128)/32)*4 + kb%4
-  return (int64_t)(row >> 7) * 128 * KP + (int64_t)(kb >> 2) * 512 + (row & 31) * 16 +
-         ((row & 127) >> 5) * 4 + (kb & 3);
-}
-
 // Routes of the unit's expert: count, and the route entry (t * R + r) of slot s.
 struct UnitRoutes {
   int n;           // live B columns (<= 8 * NT)
