@@ -332,11 +332,11 @@ struct MoeGeo {
 };
 
 // k1 (gate/up) tiling: H / 128 chunks per row split over W consumer warps of CPW chunks;
-// two chunks per warp preferred (fewer per-unit hand-overs), 4 to 16 warps.
+// two chunks per warp preferred (fewer per-unit hand-overs), 4 to 11 warps.
 bool up_tiling(int H, int& W, int& CPW) {
   const int ch1 = H / 128;
-  for (int c : {2, 1, 4})
-    if (ch1 % c == 0 && ch1 / c >= 4 && ch1 / c <= 16) {
+  for (int c : {2, 1, 4})  // producer + 2 epilogue warps + W <= kMoeUpThreads / 32
+    if (ch1 % c == 0 && ch1 / c >= 4 && ch1 / c + 3 <= fnx::kMoeUpThreads / 32) {
       CPW = c;
       W = ch1 / c;
       return true;

@@ -93,6 +93,11 @@ __host__ __device__ inline DenseLayout dense_layout(int M, int K, int W, int NS,
   return L;
 }
 
+// Block sizes the kernels are compiled for (registers per thread = 65536 / threads):
+// the MoE kernels run at most 14 (k1) and exactly 10 (k2) warps, so they may keep more
+// of each chunk's operands in flight than a 20-warp bound would allow.
+constexpr int kMoeUpThreads = 14 * 32;
+constexpr int kMoeDownThreads = 10 * 32;
 constexpr int kDenseThreadsMax = 20 * 32;  // producer + up to 3 epilogue + 16 consumer warps
 
 struct MoeArgs {

@@ -195,7 +195,7 @@ __device__ __forceinline__ int token_of(const Routing& rt, int entry) {
 // k1: act[d * 16 + s, j] = bf16(silu(g * <gate_j, x_t>) * g * <up_j, x_t>)
 // ------------------------------------------------------------------------------------
 template <int NT, int CPW>
-__global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeArgs a) {
+__global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int Q = Geo<W_NVFP4>::Q;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_up_kernel(const MoeAr
 // the route's factor and stores the partials itself, 32-byte pieces per (route, 8 rows).
 // Partials live at part[((b * P + pair) * 128) + row], P = M * (R + 1).
 template <int NT, int CPW>
-__global__ void __launch_bounds__(kDenseThreadsMax, 1) moe_down_kernel(const MoeArgs a) {
+__global__ void __launch_bounds__(kMoeDownThreads, 1) moe_down_kernel(const MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int Q = Geo<W_NVFP4>::Q;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;

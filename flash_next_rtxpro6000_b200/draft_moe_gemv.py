@@ -88,9 +88,9 @@ def unsupported_reason(*, hidden_size: int, intermediate_size: int,
     if (hidden_size // _FP4_BLOCK) % _SF_COL_GROUP or (intermediate_size // _FP4_BLOCK) % _SF_COL_GROUP:
         return "H/16 and I/16 must be multiples of 4 (no swizzle padding)"
     ch1, ch2 = hidden_size // 128, intermediate_size // 128
-    # gate/up: the consumer warps split H into ch1 chunks of 128 (8..16 warps x 1..4 chunks)
-    if not any(ch1 % c == 0 and 4 <= ch1 // c <= 16 for c in (1, 2, 4)):
-        return f"H={hidden_size}: no gate/up tiling (H/128 must be 4..16 warps x 1, 2 or 4 chunks)"
+    # gate/up: the consumer warps split H into ch1 chunks of 128 (4..11 warps x 1..4 chunks)
+    if not any(ch1 % c == 0 and 4 <= ch1 // c <= 11 for c in (1, 2, 4)):
+        return f"H={hidden_size}: no gate/up tiling (H/128 must be 4..11 warps x 1, 2 or 4 chunks)"
     # down: rt row tiles (4, 2 or 1 quadrants of a 128-row block) x (ch2 / c) k slices
     # <= 16 warps
     if not any(ch2 % c == 0 and rt * (ch2 // c) <= 16 for rt in (1, 2, 4) for c in (1, 2, 4)):
