@@ -82,3 +82,33 @@ def reference_cpu_path(x: np.ndarray, w: np.ndarray, kind: str, scale):
     W = wf * (s[:, None] if s.size > 1 else s[0])
     logits = bf16_round(np.asarray(x, dtype=np.float32) @ W.T)
     return logits, argmax_lowest(logits)
+
+
+def gated_rmsnorm(x_bf16: np.ndarray, z_bf16: np.ndarray, norm_weight: np.ndarray,
+                  group_size: int, eps: float, sigmoid_gate: bool = False,
+                  bf16_cast=bf16_round) -> np.ndarray:
+    """The fused norm prologue of w8a16_gemv_norm_gated (w8a16_gemv.py:186-190, :220-233,
+    :246-255), in fp32: every contiguous group_size slice of a row is its own RMS group,
+    y = x * rsqrt(mean(x^2) + eps) * w[k % G] * gate(z) with gate = z * sigmoid(z)
+    (silu) or sigmoid(z), cast to bf16 before the dot.  bf16_cast is round-to-nearest-even
+    (the GPU's cast); a test may pass a truncating cast to emulate the Triton CPU
+    interpreter."""
+    x = np.asarray(x_bf16, dtype=np.float32)
+    z = np.asarray(z_bf16, dtype=np.float32)
+    M, K = x.shape
+    G = group_size
+    xg = x.reshape(M, K // G, G)
+    var = (xg * xg).sum(axis=-1, dtype=np.float32) / np.float32(G)
+    rstd = (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
+    yn = xg * rstd[..., None] * np.asarray(norm_weight, dtype=np.float32)[None, None, :]
+    zg = z.reshape(M, K // G, G)
+    sig = (np.float32(1.0) / (np.float32(1.0) + np.exp(-zg))).astype(np.float32)
+    yn = yn * (sig if sigmoid_gate else zg * sig)
+    return bf16_cast(yn.reshape(M, K).astype(np.float32))
+
+
+def gemv_norm_gated(x_bf16, z_bf16, norm_weight, group_size, eps, w, kind, scale,
+                    sigmoid_gate: bool = False) -> np.ndarray:
+    """bf16 logits of (gated_rmsnorm(x, z) @ w^T) * s (w8a16_gemv.py:780-823)."""
+    xn = gated_rmsnorm(x_bf16, z_bf16, norm_weight, group_size, eps, sigmoid_gate)
+    return gemv(xn, w, kind, scale)

@@ -14,6 +14,8 @@ It imports the reference's Python modules by file path, with empty stand-ins for
 * ``swizzle.npz``       -- swizzle_blockscale_cpu (bench/bench/moe_smallm/weights.py:156-175);
 * ``moe_ref.npz``       -- moe_reference (bench/bench/moe_smallm/refs.py:50-78) on a
   small seeded layer, checkpoint row order;
+* ``w8a16_norm_gated.npz`` -- the same kernel's fused gated-RMSNorm form
+  (w8a16_gemv.py:186-259, SiLU and sigmoid gates) at M=1 and M=4 under the interpreter
 * ``w8a16_kernel.npz``  -- the reference's Triton W8A16 kernel itself
   (w8a16_gemv.py:642-666) at M=1 under the Triton CPU interpreter, int8 and fp8
   weights, per-row fp32 and bf16 scales, bf16 and fp32 destinations.
@@ -187,6 +189,49 @@ np.savez_compressed(sys.argv[3], **out)
 '''
 
 
+_INTERP_NORM = r'''
+import os, sys, numpy as np, torch
+sys.path.insert(0, os.path.dirname(sys.argv[1]))
+import make_golden as mg
+w8, w4, refs, weights = mg.load_reference(mg.Path(sys.argv[2]))
+g = torch.Generator().manual_seed(11)
+out = {}
+N, K, G = 64, 256, 128
+wi = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+sf = (torch.randn(N, generator=g).abs() / 127).float()
+nwb = (1.0 + 0.25 * torch.randn(G, generator=g)).bfloat16()
+out["w_int8"] = wi.numpy()
+out["scale_f32"] = sf.numpy()
+out["norm_w"] = nwb.float().numpy()
+# the fused gated-RMSNorm form of the reference kernel (w8a16_gemv.py:186-259), launched
+# with an explicit tile whose BLOCK_K is the norm group (the planner queries the GPU).
+# The interpreter's tl.dot on bf16 operands returns values near 1e9 even without the norm,
+# so every row runs through the M = 1 broadcast path; the tl.dot path (:214-233) applies
+# the same per-row statistics
+tile = (32, G, 1, False, None, 4, 2)
+for M in (1, 4):
+    x = (torch.randn(M, K, generator=g) * 3).bfloat16()
+    z = torch.randn(M, K, generator=g).bfloat16()
+    out[f"x{M}"] = x.float().numpy()
+    out[f"z{M}"] = z.float().numpy()
+    for sig in (False, True):
+        y = torch.zeros(M, N, dtype=torch.bfloat16)
+        for m in range(M):
+            ym = torch.zeros(1, N, dtype=torch.bfloat16)
+            w8._launch(x[m:m + 1].contiguous(), wi, sf, ym, 1, N, K, True, tile,
+                       norm=(z[m:m + 1].contiguous(), nwb, G, 1e-6, sig))
+            y[m] = ym[0]
+        out[f"y{M}_{'sigmoid' if sig else 'silu'}"] = y.float().numpy()
+np.savez_compressed(sys.argv[3], **out)
+'''
+
+
+def make_w8a16_norm_interp(ref: Path):
+    env = dict(os.environ, TRITON_INTERPRET="1", CUDA_VISIBLE_DEVICES="")
+    subprocess.run([sys.executable, "-c", _INTERP_NORM, str(Path(__file__).resolve()), str(ref),
+                    str(HERE / "w8a16_norm_gated.npz")], check=True, env=env, cwd=str(HERE))
+
+
 def make_w8a16_interp(ref: Path):
     env = dict(os.environ, TRITON_INTERPRET="1", CUDA_VISIBLE_DEVICES="")
     code = _INTERP
@@ -203,6 +248,7 @@ def main():
     make_swizzle(weights)
     make_moe(refs, w4)
     make_w8a16_interp(ref)
+    make_w8a16_norm_interp(ref)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 
