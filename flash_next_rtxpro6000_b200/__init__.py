@@ -5,6 +5,7 @@ the hand-written CUDA library ``_fnx.so``):
 
 * ``w8a16_gemv``, ``bf16_gemv``, ``w8a16_gemv_silu_mul`` -- W8A16 (int8 / fp8) GEMV,
   the lm_head and draft-head path, with fused greedy argmax;
+  ``w8a16_gemv_norm_gated`` -- the same GEMV with a gated RMSNorm on its input;
 * ``w4a16_nvfp4_gemv`` -- NVFP4 GEMV; ``quantize_nvfp4`` / ``dequantize_nvfp4`` codec;
 * ``draft_moe_gemv`` / ``moe_gemv`` -- routed NVFP4 MoE expert GEMVs (gate_up + SiLU,
   down + router-weighted route sum), M <= 16;
@@ -17,6 +18,8 @@ from .w8a16_gemv import (  # noqa: F401
     prealloc,
     scratch_slot,
     w8a16_gemv,
+    w8a16_gemv_norm_gated,
+    w8a16_gemv_norm_gated_supported,
     w8a16_gemv_silu_mul,
     w8a16_gemv_silu_mul_supported,
 )

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import POINTER, c_char_p, c_int, c_int64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_void_p
 
 from .build import LIB_PATH
 
@@ -24,6 +24,7 @@ EXPORTED = (
     "fnx_w8a16_gemv",
     "fnx_w8a16_gemv_static_ws",
     "fnx_w8a16_gemv_silu_mul",
+    "fnx_w8a16_gemv_norm_gated",
     "fnx_w4a16_nvfp4_gemv",
     "fnx_moe_workspace_bytes",
     "fnx_moe_gemv",
@@ -111,6 +112,10 @@ def _declare(lib):
     lib.fnx_w8a16_gemv_silu_mul.argtypes = [
         _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, c_int, c_int, c_int,
         POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_w8a16_gemv_norm_gated.argtypes = [
+        _P, c_int64, _P, c_int64, _P, c_int, c_int, c_float, c_int, _P, c_int64, c_int, _P,
+        c_int, _P, c_int64, c_int, c_int, c_int, c_int, POINTER(FnxGemvCfg),
+        POINTER(FnxWorkspace), c_int, _P]
     lib.fnx_w4a16_nvfp4_gemv.argtypes = [
         _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
         c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),

@@ -162,9 +162,28 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
   pdl_wait();
   // The other warps stage the activations meanwhile; the producer never waits for them.
   if (warp > 0) {
-    stage_rows<WT>(xs, unscale, M, K, [&](int r) {
-      return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
-    }, 32, blockDim.x - 32, 1);
+    // With a grid that is a multiple of ksplit, every unit of this CTA has the k split
+    // first % ksplit, so only that k range of the activations is staged.
+    constexpr int kPerChunk = WT == W_BF16 ? 32 : (WT == W_NVFP4 ? 128 : 64);
+    const int kpu = a.nch_u * kPerChunk;
+    const bool one_split = ksplit > 1 && stride % ksplit == 0;
+    int kb = one_split ? (first % ksplit) * kpu : 0;
+    int ke = one_split ? kb + kpu : K;
+    bool staged = false;
+    if constexpr (WT != W_NVFP4) {  // the fused norm is a W8A16 form
+      if (a.norm.G > 0) {
+        if (kpu % a.norm.G) kb = 0, ke = K;  // a group must not straddle the range
+        stage_rows_norm_gated<WT>(xs, unscale, M, K, kb, ke,
+                                  reinterpret_cast<const __nv_bfloat16*>(a.x), a.ldx, a.norm, 32,
+                                  blockDim.x - 32, 1);
+        staged = true;
+      }
+    }
+    if (!staged) {
+      stage_rows<WT>(xs, unscale, M, K, kb, ke, [&](int r) {
+        return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
+      }, 32, blockDim.x - 32, 1);
+    }
     group_sync(1, blockDim.x - 32);
   }
 
@@ -325,10 +344,16 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
               s1.x += pv[j + 1].x; s1.y += pv[j + 1].y; s1.z += pv[j + 1].z; s1.w += pv[j + 1].w;
             }
           }
-          v[rt][nt][0] = s0.x + s1.x;
-          v[rt][nt][1] = s0.y + s1.y;
-          v[rt][nt][2] = s0.z + s1.z;
-          v[rt][nt][3] = s0.w + s1.w;
+          // times this CTA's power-of-two unscale of each token (exact): CTAs that
+          // staged different k ranges have their own, so split sums are published
+          // unscaled; 0 for the padding tokens
+          const int tok = nt * 8 + 2 * c;
+          const float u0 = tok < M ? unscale[tok] : 0.f;
+          const float u1 = tok + 1 < M ? unscale[tok + 1] : 0.f;
+          v[rt][nt][0] = (s0.x + s1.x) * u0;
+          v[rt][nt][1] = (s0.y + s1.y) * u1;
+          v[rt][nt][2] = (s0.z + s1.z) * u0;
+          v[rt][nt][3] = (s0.w + s1.w) * u1;
         }
       }
       __syncwarp();
@@ -336,8 +361,8 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
 
       bool finish = true;
       if (ksplit > 1) {
-        // Split-K fix-up: publish this split's tile sums; the last split sums all of
-        // them in split order and resets the counter.
+        // Split-K fix-up: publish this split's tile sums (already unscaled); the last
+        // split sums them in split order and resets the counter.
         float* wsp = a.ws + ((size_t)tg * ksplit + ks) * RT * 256;
 #pragma unroll
         for (int rt = 0; rt < kMaxRT; ++rt) {
@@ -383,7 +408,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
             for (int p = 0; p < 2; ++p) {
               const int tok = nt * 8 + 2 * c + p;
               const bool tok_ok = tok < M;
-              const float us = tok_ok ? unscale[tok] : 0.f;
+              const float us = tok_ok ? 1.f : 0.f;  // the sums are unscaled already
               if (silu) {
                 // physical rows < 8 are gate, >= 8 up; both hold column t*8 + g
                 const int n = t * 8 + g;

@@ -218,6 +218,7 @@ struct DenseCall {
   const fnx_workspace* ws;
   int pdl;
   cudaStream_t stream;
+  fnx::NormGate norm;  // gated RMSNorm on the activation load (norm.G > 0)
 };
 
 int run_dense(const DenseCall& c) {
@@ -275,6 +276,9 @@ int run_dense(const DenseCall& c) {
     const int occ = fnx::dense_occupancy(c.wt, NT, p.CPW, threads, p.smem);
     if (occ <= 0) return fail(FNX_EUNSUPPORTED, "kernel does not fit on an SM (smem %zu)", p.smem);
     grid = (int)std::min<int64_t>(p.n_units, (int64_t)fnx::num_sms() * occ);
+    // A multiple of ksplit keeps each CTA on one k split, so it stages only that k
+    // range of the activations (n_units is a multiple already).
+    if (p.ksplit > 1 && grid > p.ksplit) grid -= grid % p.ksplit;
   }
 
   fnx::DenseArgs a = {};
@@ -317,6 +321,7 @@ int run_dense(const DenseCall& c) {
   a.tile_groups = p.tile_groups;
   a.n_units = p.n_units;
   a.pdl = c.pdl;
+  a.norm = c.norm;
   rc = fnx::launch_dense(a, c.wt, NT, p.CPW, grid, p.smem, c.stream);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no kernel instance for this configuration");
   if (rc) return cuda_fail("dense GEMV launch");
@@ -505,6 +510,40 @@ int fnx_w8a16_gemv_silu_mul(const void* x, int64_t ldx, const void* w, int64_t l
   DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, nullptr, 0,
                  0, 0, nullptr, nullptr, 0, M, H, K, 1, cfg, ws, pdl,
                  static_cast<cudaStream_t>(stream)};
+  return run_dense(c);
+}
+
+int fnx_w8a16_gemv_norm_gated(const void* x, int64_t ldx, const void* z, int64_t ldz,
+                              const void* norm_weight, int norm_weight_f32, int group_size,
+                              float eps, int sigmoid_gate, const void* w, int64_t ldw,
+                              int w_dtype, const void* scale, int scale_kind, void* y,
+                              int64_t ldy, int out_f32, int M, int N, int K,
+                              const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                              fnx_stream_t stream) {
+  g_err.clear();
+  if (w_dtype != FNX_W_INT8 && w_dtype != FNX_W_FP8_E4M3 && w_dtype != FNX_W_BF16)
+    return fail(FNX_EINVAL, "fnx_w8a16_gemv_norm_gated: w_dtype must be int8, fp8_e4m3 or bf16");
+  const int G = group_size;
+  if (G <= 0 || K <= 0 || K % (G > 0 ? G : 1))
+    return fail(FNX_EINVAL, "K=%d must be a positive multiple of group_size=%d", K, G);
+  if (G < 8 || G > 256 || (G & (G - 1)))
+    return fail(FNX_EUNSUPPORTED, "group_size=%d: the fused norm takes powers of two in [8, 256]",
+                G);
+  if (!z || !aligned(z, 16) || (ldz * 2) % 16 || ldz < K)
+    return fail(FNX_EINVAL, "z rows must be 16-byte aligned with ldz >= K");
+  if (!norm_weight || !aligned(norm_weight, 16))
+    return fail(FNX_EINVAL, "norm_weight must be a 16-byte aligned [group_size] vector");
+  if (!(eps >= 0.f)) return fail(FNX_EINVAL, "eps must be >= 0");
+  DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, nullptr, 0,
+                 0, out_f32, nullptr, nullptr, 0, M, N, K, 0, cfg, ws, pdl,
+                 static_cast<cudaStream_t>(stream)};
+  c.norm.z = static_cast<const __nv_bfloat16*>(z);
+  c.norm.ldz = ldz;
+  c.norm.w = norm_weight;
+  c.norm.w_f32 = norm_weight_f32 ? 1 : 0;
+  c.norm.G = G;
+  c.norm.eps = eps;
+  c.norm.sigmoid = sigmoid_gate ? 1 : 0;
   return run_dense(c);
 }
 

@@ -370,93 +370,211 @@ __device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
   return v;
 }
 
-// Stage `nrows` activation rows of K bf16 into shared memory in the fragment order above.
-// Row r is read from src(r) (a bf16 pointer, or nullptr for a row that is never used).
-// Pass 1 finds each row's max |x|, pass 2 converts with the row's power of two (fp16),
-// or the rows are copied unchanged (bf16 weights).  unscale[r] receives the inverse
-// power of two that the epilogue applies.  Reads use ld.global.cg: the rows may have
-// been written by the previous kernel of a programmatic-dependent pair.  Callers
-// synchronise the participating threads (named barrier bar_id) after the call.
-template <int WT, typename SrcFn>
-__device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int K,
-                                           SrcFn src, int t0, int nth, int bar_id) {
-  // Threads t0 .. t0 + nth - 1 (whole warps) take part and synchronise on named barrier
-  // bar_id; each 16-byte unit of the nrows x K block is one work item, so the loads of a
-  // row are in flight together.  unscale[] has room for 2 x 16 words: [16, 32) collects
-  // the row maxima as float bits (non-negative floats order like their bits).
+// The two-pass fp16 staging of the columns [kb, ke) of activation rows (multiples of 8)
+// from produced 16-byte units.  Work item idx is row r = idx / ((ke - kb) / 8) and unit
+// u = kb / 8 + idx % ((ke - kb) / 8); unit(in, r, u) returns its 8 bf16 values (zeros
+// when in is false, past the last item).  Every lane of a warp calls it together, on 32
+// consecutive items starting at a multiple of 32, so it may use warp shuffles.  Pass 1
+// finds each row's max |value| over the range, pass 2 converts with the row's power of
+// two (fp16) into the full-K row layout; unscale[r] receives the inverse power of two
+// that the epilogue applies, or 0 where has_row(r) is false.  Threads t0 .. t0 + nth - 1
+// (whole warps) take part and synchronise on named barrier bar_id; unscale[] has room for
+// 2 x 16 words: [16, 32) collects the row maxima as float bits (non-negative floats
+// order like their bits).
+template <int WT, typename RowFn, typename UnitFn>
+__device__ __forceinline__ void stage_units_f16(uint8_t* xs, float* unscale, int nrows, int K,
+                                                int kb, int ke, RowFn has_row, UnitFn unit,
+                                                int t0, int nth, int bar_id) {
   const int tid = threadIdx.x - t0, lane = threadIdx.x & 31;
   const int srow = stage_row_bytes(K);
-  const int units = K >> 3;
-  const int total = nrows * units;
-  if constexpr (WT == W_BF16) {
-    for (int idx = tid; idx < total; idx += nth) {
-      const int r = idx / units, u = idx - r * units;
-      const __nv_bfloat16* p = src(r);
-      const uint4 v = p ? ldg_cg_u4(p + 8 * u) : make_uint4(0u, 0u, 0u, 0u);
-      *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) = v;
+  const int upr = (ke - kb) >> 3, u0 = kb >> 3;
+  const int total = nrows * upr;
+  unsigned* smax = reinterpret_cast<unsigned*>(unscale + 16);
+  for (int r = tid; r < nrows; r += nth) smax[r] = 0u;
+  group_sync(bar_id, nth);
+  auto at = [&](int idx) -> uint4 {
+    const bool in = idx < total;
+    const int r = in ? idx / upr : 0;
+    return unit(in, r, u0 + (in ? idx - r * upr : 0));
+  };
+  constexpr int kHold = 4;  // units kept in registers between the two passes
+  const int wbase = tid - lane;  // first work item of this warp (warp-uniform loops)
+  uint4 held[kHold];
+  // Row maximum of one unit per lane: one atomic per warp when the warp's units all
+  // lie in one row, else one per lane.
+  auto row_max = [&](int idx, const uint4 v) {
+    const int r = idx < total ? idx / upr : -1;
+    unsigned bits = __float_as_uint(bf16x8_absmax(v));
+    const int r0 = __shfl_sync(0xffffffffu, r, 0);
+    if (__all_sync(0xffffffffu, r == r0)) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+      if (lane == 0 && r0 >= 0) atomicMax(&smax[r0], bits);
+    } else if (r >= 0) {
+      atomicMax(&smax[r], bits);
     }
-    for (int r = tid; r < nrows; r += nth) unscale[r] = src(r) ? 1.f : 0.f;
-    return;
-  } else {
-    unsigned* smax = reinterpret_cast<unsigned*>(unscale + 16);
-    for (int r = tid; r < nrows; r += nth) smax[r] = 0u;
-    group_sync(bar_id, nth);
-    constexpr int kHold = 4;  // units kept in registers between the two passes
-    const int wbase = tid - lane;  // first work item of this warp (warp-uniform loops)
-    uint4 held[kHold];
-    auto load = [&](int idx) -> uint4 {
-      if (idx >= total) return make_uint4(0u, 0u, 0u, 0u);
-      const int r = idx / units;
-      const __nv_bfloat16* p = src(r);
-      return p ? ldg_cg_u4(p + 8 * (idx - r * units)) : make_uint4(0u, 0u, 0u, 0u);
-    };
-    // Row maximum of one unit per lane: one atomic per warp when the warp's units all
-    // lie in one row, else one per lane.
-    auto row_max = [&](int idx, const uint4 v) {
-      const int r = idx < total ? idx / units : -1;
-      unsigned bits = __float_as_uint(bf16x8_absmax(v));
-      const int r0 = __shfl_sync(0xffffffffu, r, 0);
-      if (__all_sync(0xffffffffu, r == r0)) {
+  };
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
-        if (lane == 0 && r0 >= 0) atomicMax(&smax[r0], bits);
-      } else if (r >= 0) {
-        atomicMax(&smax[r], bits);
-      }
-    };
+  for (int j = 0; j < kHold; ++j) held[j] = at(tid + j * nth);
 #pragma unroll
-    for (int j = 0; j < kHold; ++j) held[j] = load(tid + j * nth);
+  for (int j = 0; j < kHold; ++j)
+    if (wbase + j * nth < total) row_max(tid + j * nth, held[j]);
+  for (int b = wbase + kHold * nth; b < total; b += kHold * nth) {  // batches of kHold
+    uint4 v[kHold];
+#pragma unroll
+    for (int j = 0; j < kHold; ++j) v[j] = at(b + lane + j * nth);
 #pragma unroll
     for (int j = 0; j < kHold; ++j)
-      if (wbase + j * nth < total) row_max(tid + j * nth, held[j]);
-    for (int b = wbase + kHold * nth; b < total; b += kHold * nth) {  // batches of kHold
-      uint4 v[kHold];
-#pragma unroll
-      for (int j = 0; j < kHold; ++j) v[j] = load(b + lane + j * nth);
-#pragma unroll
-      for (int j = 0; j < kHold; ++j)
-        if (b + j * nth < total) row_max(b + lane + j * nth, v[j]);
-    }
-    group_sync(bar_id, nth);
-    auto put = [&](int idx, const uint4 v) {
-      if (idx >= total) return;
-      const int r = idx / units, u = idx - r * units;
-      const int e = stage_exponent(__uint_as_float(smax[r]));
-      *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) =
-          bf16x8_to_f16x8_scaled(v, e);
-    };
-#pragma unroll
-    for (int j = 0; j < kHold; ++j) put(tid + j * nth, held[j]);
-    for (int b = tid + kHold * nth; b < total; b += kHold * nth) {
-      uint4 v[kHold];
-#pragma unroll
-      for (int j = 0; j < kHold; ++j) v[j] = load(b + j * nth);
-#pragma unroll
-      for (int j = 0; j < kHold; ++j) put(b + j * nth, v[j]);
-    }
-    for (int r = tid; r < nrows; r += nth)
-      unscale[r] = src(r) ? pow2f(-stage_exponent(__uint_as_float(smax[r]))) : 0.f;
+      if (b + j * nth < total) row_max(b + lane + j * nth, v[j]);
   }
+  group_sync(bar_id, nth);
+  auto put = [&](int idx, const uint4 v) {
+    if (idx >= total) return;
+    const int r = idx / upr, u = u0 + idx - r * upr;
+    const int e = stage_exponent(__uint_as_float(smax[r]));
+    *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) =
+        bf16x8_to_f16x8_scaled(v, e);
+  };
+#pragma unroll
+  for (int j = 0; j < kHold; ++j) put(tid + j * nth, held[j]);
+  for (int b = wbase + kHold * nth; b < total; b += kHold * nth) {
+    uint4 v[kHold];
+#pragma unroll
+    for (int j = 0; j < kHold; ++j) v[j] = at(b + lane + j * nth);
+#pragma unroll
+    for (int j = 0; j < kHold; ++j) put(b + lane + j * nth, v[j]);
+  }
+  for (int r = tid; r < nrows; r += nth)
+    unscale[r] = has_row(r) ? pow2f(-stage_exponent(__uint_as_float(smax[r]))) : 0.f;
+}
+
+// The bf16 form (bf16 weights): the units are copied unchanged, unscale[r] = 1 (or 0).
+template <int WT, typename RowFn, typename UnitFn>
+__device__ __forceinline__ void stage_units_bf16(uint8_t* xs, float* unscale, int nrows, int K,
+                                                 int kb, int ke, RowFn has_row, UnitFn unit,
+                                                 int t0, int nth) {
+  const int tid = threadIdx.x - t0, lane = threadIdx.x & 31;
+  const int srow = stage_row_bytes(K);
+  const int upr = (ke - kb) >> 3, u0 = kb >> 3;
+  const int total = nrows * upr;
+  for (int b = tid - lane; b < total; b += nth) {  // warp-uniform: unit() may shuffle
+    const int idx = b + lane;
+    const bool in = idx < total;
+    const int r = in ? idx / upr : 0;
+    const int u = u0 + (in ? idx - r * upr : 0);
+    const uint4 v = unit(in, r, u);
+    if (in) *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) = v;
+  }
+  for (int r = tid; r < nrows; r += nth) unscale[r] = has_row(r) ? 1.f : 0.f;
+}
+
+// Stage the columns [kb, ke) of `nrows` activation rows of K bf16 into shared memory in
+// the fragment order above.  Row r is read from src(r) (a bf16 pointer, or nullptr for a
+// row that is never used): converted to fp16 with the row's power of two
+// (stage_units_f16), or copied unchanged (bf16 weights).  Reads use ld.global.cg: the
+// rows may have been written by the previous kernel of a programmatic-dependent pair.
+// Callers synchronise the participating threads (named barrier bar_id) after the call.
+template <int WT, typename SrcFn>
+__device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int K,
+                                           int kb, int ke, SrcFn src, int t0, int nth,
+                                           int bar_id) {
+  auto has_row = [&](int r) { return src(r) != nullptr; };
+  auto unit = [&](bool in, int r, int u) -> uint4 {
+    const __nv_bfloat16* p = in ? src(r) : nullptr;
+    return p ? ldg_cg_u4(p + 8 * u) : make_uint4(0u, 0u, 0u, 0u);
+  };
+  if constexpr (WT == W_BF16)
+    stage_units_bf16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth);
+  else
+    stage_units_f16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth, bar_id);
+}
+
+// Gated RMSNorm folded into the activation load (the prologue of w8a16_gemv_norm_gated,
+// w8a16_gemv.py:186-190, :220-233, :246-255): every contiguous G-value slice of a row is
+// one RMS group and y = x * rsqrt(sum(x^2) / G + eps) * w[k % G] * gate(z), with
+// gate(z) = z * sigmoid(z) (silu) or sigmoid(z), cast to bf16 (round to nearest even)
+// before the dot.  G is a power of two in [8, 256].
+struct NormGate {
+  const __nv_bfloat16* z;  // [M, K] bf16 gates, row stride ldz elements
+  int64_t ldz;
+  const void* w;           // [G] norm weight, bf16 or fp32 (w_f32)
+  int w_f32;
+  int G;
+  float eps;
+  int sigmoid;
+};
+
+// One 16-byte unit (8 values at row offset k0) of the normalised row.  All 32 lanes call
+// it together on 32 consecutive units starting at a multiple of 32: a group's G/8 units
+// are then G/8 consecutive lanes, which add their sums of squares with shuffles.
+__device__ __forceinline__ uint4 norm_gated_unit(const uint4 xv, const uint4 zv, int k0,
+                                                 const NormGate& ng) {
+  const uint32_t xin[4] = {xv.x, xv.y, xv.z, xv.w};
+  const uint32_t zin[4] = {zv.x, zv.y, zv.z, zv.w};
+  float xf[8], zf[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    xf[2 * i] = bf16_bits_to_f32(xin[i] & 0xFFFFu);
+    xf[2 * i + 1] = bf16_bits_to_f32(xin[i] >> 16);
+    zf[2 * i] = bf16_bits_to_f32(zin[i] & 0xFFFFu);
+    zf[2 * i + 1] = bf16_bits_to_f32(zin[i] >> 16);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(xf[i], xf[i], ss);
+  for (int o = 1; o < (ng.G >> 3); o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = rsqrtf(ss * (1.f / (float)ng.G) + ng.eps);  // 1/G is exact
+  const int kw = k0 & (ng.G - 1);
+  float nw[8];
+  if (ng.w_f32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(ng.w) + (kw >> 2));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(ng.w) + (kw >> 2) + 1);
+    nw[0] = a.x; nw[1] = a.y; nw[2] = a.z; nw[3] = a.w;
+    nw[4] = b.x; nw[5] = b.y; nw[6] = b.z; nw[7] = b.w;
+  } else {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(ng.w) + (kw >> 3));
+    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      nw[2 * i] = bf16_bits_to_f32(in[i] & 0xFFFFu);
+      nw[2 * i + 1] = bf16_bits_to_f32(in[i] >> 16);
+    }
+  }
+  uint32_t out[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float y[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float z = zf[2 * i + h];
+      const float sg = 1.f / (1.f + expf(-z));
+      y[h] = xf[2 * i + h] * rstd * nw[2 * i + h] * (ng.sigmoid ? sg : z * sg);
+    }
+    const __nv_bfloat162 b = __floats2bfloat162_rn(y[0], y[1]);
+    out[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// stage_rows for the first nrows rows of x, normalised and gated on the way in; kb and
+// ke are multiples of the group size.
+template <int WT>
+__device__ __forceinline__ void stage_rows_norm_gated(uint8_t* xs, float* unscale, int nrows,
+                                                      int K, int kb, int ke,
+                                                      const __nv_bfloat16* x, int64_t ldx,
+                                                      const NormGate& ng, int t0, int nth,
+                                                      int bar_id) {
+  auto has_row = [](int) { return true; };
+  auto unit = [&](bool in, int r, int u) -> uint4 {
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    const uint4 xv = in ? ldg_cg_u4(x + (size_t)r * ldx + 8 * u) : zero;
+    const uint4 zv = in ? ldg_cg_u4(ng.z + (size_t)r * ng.ldz + 8 * u) : zero;
+    return norm_gated_unit(xv, zv, 8 * u, ng);
+  };
+  if constexpr (WT == W_BF16)
+    stage_units_bf16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth);
+  else
+    stage_units_f16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth, bar_id);
 }
 
 // ------------------------------------------------------------------------------------

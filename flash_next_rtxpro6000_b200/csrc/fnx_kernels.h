@@ -48,6 +48,7 @@ struct DenseArgs {
   int tile_groups;        // ceil(row_tiles / RT)
   int n_units;            // tile_groups * ksplit
   int pdl;
+  NormGate norm;          // gated RMSNorm on the activation load (norm.G > 0), else off
 };
 
 // One stage of the dense weight ring: RT tiles of weights, then the unit's row scales

@@ -315,6 +315,96 @@ def w8a16_gemv_silu_mul_supported(x: torch.Tensor, w: torch.Tensor, scale: torch
     )
 
 
+#: The fused gated-RMSNorm prologue (the reference's SGLANG_NORM_INTO_GEMV switch,
+#: w8a16_gemv.py:670-691, off by default there); on by default here.
+NORM_INTO_GEMV = _env_flag("FNX_NORM_INTO_GEMV", "1")
+
+
+def _norm_group_ok(G: int) -> bool:
+    return 8 <= G <= 256 and (G & (G - 1)) == 0
+
+
+def w8a16_gemv_norm_gated_supported(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor,
+                                    z: torch.Tensor, norm_weight: torch.Tensor,
+                                    group_size: int) -> bool:
+    """Whether this call can take the fused gated-RMSNorm + GEMV path
+    (w8a16_gemv.py:748-777); the group is also a power of two in [8, 256] here, the
+    reference's BLOCK_K == group_size tiles."""
+    K = x.shape[-1] if x.dim() == 2 else -1
+    return bool(
+        NORM_INTO_GEMV
+        and x.is_cuda
+        and x.dim() == 2
+        and x.dtype == torch.bfloat16
+        and z.dtype == torch.bfloat16
+        and 1 <= x.shape[0] <= 16
+        and tuple(z.shape) == tuple(x.shape)
+        and x.stride(1) == 1
+        and z.stride(1) == 1
+        and group_size > 0
+        and K % group_size == 0
+        and _norm_group_ok(group_size)
+        and norm_weight.dtype in (torch.bfloat16, torch.float32)
+        and norm_weight.numel() == group_size
+        and norm_weight.is_contiguous()
+        and w.dim() == 2
+        and w.dtype in (torch.int8, torch.float8_e4m3fn, torch.bfloat16)
+        and w.shape[1] == K
+        and w.stride(1) == 1
+        and scale.numel() == w.shape[0]
+    )
+
+
+def w8a16_gemv_norm_gated(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    scale: torch.Tensor,
+    z: torch.Tensor,
+    norm_weight: torch.Tensor,
+    group_size: int,
+    eps: float,
+    sigmoid_gate: bool = False,
+    out: Optional[torch.Tensor] = None,
+    cfg=None,
+    pdl: Optional[bool] = None,
+) -> torch.Tensor:
+    """``(gated_rms_norm(x, z) @ w^T) * scale`` in one launch (w8a16_gemv.py:780-823).
+
+    ``x``/``z`` are [M, K] bf16 with K a multiple of ``group_size``; each contiguous
+    ``group_size`` slice of a row is its own RMS group (RMSNormGated(group_size,
+    norm_before_gate=True) on the [M * K / group_size, group_size] reshape), the gate is
+    z * sigmoid(z), or sigmoid(z) with ``sigmoid_gate``; the normalised row is rounded to
+    bf16 before the dot.  ``norm_weight``: [group_size] bf16 or fp32, passed untouched.
+    """
+    M, K = x.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and M <= 16
+    if tuple(z.shape) != (M, K) or z.dtype != torch.bfloat16:
+        raise ValueError(f"z must be a bf16 [{M}, {K}] tensor; got {tuple(z.shape)} {z.dtype}")
+    if norm_weight.dtype not in (torch.bfloat16, torch.float32) or \
+            norm_weight.numel() != group_size:
+        raise ValueError(f"norm_weight must be a bf16/fp32 [{group_size}] vector")
+    if w.stride(1) != 1:
+        raise ValueError("w8a16 gemv needs a K-contiguous [N, K] weight (stride(1) == 1)")
+    y = _out_or_new(out, M, N, x.device)
+    x = _activation(x)
+    z = _activation(z)
+    nw = norm_weight.reshape(-1)
+    if not nw.is_contiguous() or nw.data_ptr() % 16:
+        nw = nw.contiguous().clone()
+    s, skind = _scale_kind(scale, N)
+    ws = _workspace(x.device)
+    c = _cfg(cfg)
+    rc = _lib.lib().fnx_w8a16_gemv_norm_gated(
+        ptr(x), x.stride(0), ptr(z), z.stride(0), ptr(nw), int(nw.dtype == torch.float32),
+        int(group_size), float(eps), int(bool(sigmoid_gate)), ptr(w),
+        w.stride(0) * w.element_size(), _weight_kind(w), ptr(s), skind, ptr(y), y.stride(0),
+        int(y.dtype == torch.float32), M, N, K, None if c is None else ctypes_byref(c),
+        ctypes_byref(ws.c), int(PDL if pdl is None else pdl), _stream(x))
+    check(rc, "w8a16_gemv_norm_gated")
+    return y
+
+
 def plan(M: int, N: int, K: int, w_dtype: torch.dtype, fused_silu: bool = False) -> GemvConfig:
     """The geometry the library's planner picks for a call."""
     c = FnxGemvCfg()

@@ -16,6 +16,8 @@
  *   fnx_w8a16_gemv           kernels/sglang/srt/layers/quantization/w8a16_gemv.py:642-666
  *                            (w8a16_gemv) and :826-847 (bf16_gemv, w_dtype FNX_W_BF16)
  *   fnx_w8a16_gemv_silu_mul  w8a16_gemv.py:1009-1061 (w8a16_gemv_silu_mul)
+ *   fnx_w8a16_gemv_norm_gated  w8a16_gemv.py:780-823 (w8a16_gemv_norm_gated; the norm
+ *                            prologue of the kernel at :186-190, :220-233, :246-255)
  *   fnx_w4a16_nvfp4_gemv     kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:342-401
  *   fnx_moe_gemv             patches/sglang/series/0112-DG1-one-token-draft-MoE-as-a-W4A16-
  *                            NVFP4-Triton-GEMV.patch:328-386 (draft_moe_gemv), generalised
@@ -129,6 +131,26 @@ int fnx_w8a16_gemv_silu_mul(const void* x, int64_t ldx, const void* w, int64_t l
                             int w_dtype, const void* scale, int scale_kind, void* y,
                             int64_t ldy, int M, int H, int K, const fnx_gemv_cfg* cfg,
                             const fnx_workspace* ws, int pdl, fnx_stream_t stream);
+
+/*
+ * y = (gated_rms_norm(x, z) @ w^T) * scale in one launch.  x, z: bf16 [M, K], rows
+ * 16-byte aligned (strides ldx, ldz elements).  Each contiguous group_size slice of a
+ * row is its own RMS group (RMSNormGated(group_size, norm_before_gate=True)):
+ *   xn[m, k] = bf16( x[m, k] * rsqrt(mean_group(x^2) + eps) * norm_weight[k % G] * gate )
+ *   gate = z * sigmoid(z) (sigmoid_gate == 0, silu) or sigmoid(z) (sigmoid_gate != 0)
+ * norm_weight: [group_size] bf16 (norm_weight_f32 == 0) or fp32, 16-byte aligned.
+ * group_size: a power of two in [8, 256] dividing K (FNX_EUNSUPPORTED otherwise).
+ * y: bf16, or fp32 holding bf16-rounded values (out_f32), [M, ldy].  Remaining
+ * arguments as fnx_w8a16_gemv; the split-K workspace need is fnx_gemv_workspace_need's
+ * for the same M, N, K and w_dtype.
+ */
+int fnx_w8a16_gemv_norm_gated(const void* x, int64_t ldx, const void* z, int64_t ldz,
+                              const void* norm_weight, int norm_weight_f32, int group_size,
+                              float eps, int sigmoid_gate, const void* w, int64_t ldw,
+                              int w_dtype, const void* scale, int scale_kind, void* y,
+                              int64_t ldy, int out_f32, int M, int N, int K,
+                              const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                              fnx_stream_t stream);
 
 /*
  * y[m, n] = bf16( (sum_k e2m1(wq[n, k]) * e4m3(bs[n, k / 16]) * x[m, k]) * gscale )

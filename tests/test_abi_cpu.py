@@ -100,3 +100,30 @@ def test_moe_workspace_bytes():
     assert _lib.lib().fnx_moe_workspace_bytes(16, 10, 512, 2048, 512, ctypes.byref(z)) == 0
     P = 16 * 11
     assert (z.act, z.partials) == (161 * 16 * (2 * 512 + 64), P * 2048 * 4)
+
+
+def _norm_gated(**kw):
+    args = dict(x=16, ldx=2048, z=16, ldz=2048, nw=16, nw32=0, G=128, eps=1e-6, sig=0, w=16,
+                ldw=2048, wt=_lib.W_FP8_E4M3, s=16, sk=_lib.SCALE_F32_ROW, y=16, ldy=1024,
+                f32=0, M=1, N=1024, K=2048, cfg=None, ws=None, pdl=0, stream=None)
+    args.update(kw)
+    return _lib.lib().fnx_w8a16_gemv_norm_gated(*args.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(G=96, K=384, ldx=384, ldz=384, ldw=384), _lib.FNX_EUNSUPPORTED),
+    (dict(G=512), _lib.FNX_EUNSUPPORTED),
+    (dict(G=4), _lib.FNX_EUNSUPPORTED),
+    (dict(G=0), _lib.FNX_EINVAL),
+    (dict(G=128, K=2000, ldx=2000, ldz=2000, ldw=2000), _lib.FNX_EINVAL),
+    (dict(z=None), _lib.FNX_EINVAL),
+    (dict(z=8), _lib.FNX_EINVAL),                # misaligned gate rows
+    (dict(ldz=1024), _lib.FNX_EINVAL),
+    (dict(nw=None), _lib.FNX_EINVAL),
+    (dict(eps=-1.0), _lib.FNX_EINVAL),
+    (dict(wt=_lib.W_NVFP4), _lib.FNX_EINVAL),
+    (dict(M=17), _lib.FNX_EINVAL),
+])
+def test_norm_gated_invalid_arguments_are_rejected(kw, code):
+    assert _norm_gated(**kw) == code
+    assert _lib.last_error()
