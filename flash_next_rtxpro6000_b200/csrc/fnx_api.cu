@@ -85,6 +85,7 @@ constexpr size_t kMaxSmem = 227 * 1024;
 // ring has NS stages of RT tiles of TILE bytes (two 8-row halves, see tile_half_offset).
 struct DensePlan {
   int ksplit, W, RT, CPW, NS, E, UB, TILE, nch_u, row_tiles, tile_groups, n_units, wt;
+  int xslice;  // each CTA stages only its k split (needs a grid that is a multiple of ksplit)
   size_t smem;
 };
 
@@ -108,11 +109,12 @@ bool layout_fits(int M, int K, int NT, DensePlan& p) {
   p.tile_groups = (p.row_tiles + p.RT - 1) / p.RT;
   p.n_units = p.tile_groups * p.ksplit;
   const int stage = fnx::dense_stage(p.wt == FNX_W_NVFP4, p.RT, p.TILE, p.nch_u).bytes;
-  const fnx::DenseLayout L0 = fnx::dense_layout(M, K, p.W, 0, p.E, NT, stage);
+  const int kx = p.xslice ? p.nch_u * chunk_k(p.wt) : K;  // staged activation columns
+  const fnx::DenseLayout L0 = fnx::dense_layout(M, kx, p.W, 0, p.E, NT, stage);
   if ((size_t)L0.total + 2 * (size_t)stage + 256 > kMaxSmem) return false;
   const int ns = (int)((kMaxSmem - L0.total - 256) / stage);
   p.NS = std::max(2, std::min(ns, 8));
-  p.smem = fnx::dense_layout(M, K, p.W, p.NS, p.E, NT, stage).total;
+  p.smem = fnx::dense_layout(M, kx, p.W, p.NS, p.E, NT, stage).total;
   return true;
 }
 
@@ -139,6 +141,7 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
     if (p.ksplit < 1 || nch % p.ksplit)
       return fail(FNX_EINVAL, "ksplit=%d must divide K/%d = %d", p.ksplit, CH, nch);
     p.nch_u = nch / p.ksplit;
+    p.xslice = p.ksplit > 1 ? 1 : 0;  // run_dense drops it where the grid does not allow it
     if (p.W < 1 || p.W > 16 || p.RT > 4 || p.W % p.RT ||
         (p.CPW != 1 && p.CPW != 2 && p.CPW != 4 && p.CPW != 8) || (p.W / p.RT) * p.CPW != p.nch_u)
       return fail(FNX_EINVAL,
@@ -156,7 +159,7 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
   double best_cost = 1e30;
   DensePlan best = p;
   bool found = false;
-  for (int k = 1; k <= nch; ++k) {
+  for (int k = 1; k <= nch && k <= sms; ++k) {  // k <= sms: the grid rounds to a multiple
     if (nch % k) continue;
     const int nu = nch / k;
     for (int rt : {1, 2, 4}) {
@@ -170,6 +173,7 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
         q.W = w;
         q.CPW = cpw;
         q.RT = rt;
+        q.xslice = k > 1 ? 1 : 0;
         if (!layout_plan(M, K, NT, q)) continue;
         // several tiles per unit only while every SM still gets two units or more:
         // small problems are latency-bound and want the most parallel units
@@ -270,15 +274,34 @@ int run_dense(const DenseCall& c) {
   if (want_argmax && (!c.ws || !c.ws->argmax_keys || !c.ws->argmax_count))
     return fail(FNX_EINVAL, "argmax needs the workspace's argmax_keys/argmax_count");
 
-  const int threads = (p.W + 1 + p.E) * 32;
-  int grid = c.cfg && c.cfg->grid > 0 ? c.cfg->grid : 0;
+  // xslice (each CTA stages only its k split) needs a grid that is a multiple of ksplit
+  // and, with the fused norm, a unit k extent that holds whole norm groups; otherwise
+  // the full rows are staged (same tiling and workspace, larger shared memory).
+  const int user_grid = c.cfg && c.cfg->grid > 0 ? c.cfg->grid : 0;
+  auto full_rows = [&]() -> int {
+    p.xslice = 0;
+    if (!layout_plan(c.M, c.K, NT, p))
+      return fail(FNX_EUNSUPPORTED, "shared memory: M=%d K=%d leaves no room for 2 stages",
+                  c.M, c.K);
+    return FNX_OK;
+  };
+  if (p.xslice && ((c.norm.G > 0 && (p.nch_u * chunk_k(c.wt)) % c.norm.G) ||
+                   (user_grid > 0 && user_grid % p.ksplit)))
+    if (int e = full_rows()) return e;
+  int grid = user_grid;
   if (grid <= 0) {
-    const int occ = fnx::dense_occupancy(c.wt, NT, p.CPW, threads, p.smem);
-    if (occ <= 0) return fail(FNX_EUNSUPPORTED, "kernel does not fit on an SM (smem %zu)", p.smem);
-    grid = (int)std::min<int64_t>(p.n_units, (int64_t)fnx::num_sms() * occ);
-    // A multiple of ksplit keeps each CTA on one k split, so it stages only that k
-    // range of the activations (n_units is a multiple already).
-    if (p.ksplit > 1 && grid > p.ksplit) grid -= grid % p.ksplit;
+    for (int pass = 0; pass < 2; ++pass) {
+      const int mode = c.norm.G > 0 ? fnx::DENSE_NORM
+                                    : (p.xslice ? fnx::DENSE_SLICE : fnx::DENSE_PLAIN);
+      const int occ = fnx::dense_occupancy(c.wt, NT, p.CPW, mode, (p.W + 1 + p.E) * 32, p.smem);
+      if (occ <= 0)
+        return fail(FNX_EUNSUPPORTED, "kernel does not fit on an SM (smem %zu)", p.smem);
+      grid = (int)std::min<int64_t>(p.n_units, (int64_t)fnx::num_sms() * occ);
+      if (!p.xslice) break;
+      if (grid > p.ksplit) grid -= grid % p.ksplit;  // n_units is a multiple of ksplit
+      if (grid % p.ksplit == 0) break;
+      if (int e = full_rows()) return e;  // fewer resident CTAs than k splits
+    }
   }
 
   fnx::DenseArgs a = {};
@@ -322,6 +345,7 @@ int run_dense(const DenseCall& c) {
   a.n_units = p.n_units;
   a.pdl = c.pdl;
   a.norm = c.norm;
+  a.xslice = p.xslice;
   rc = fnx::launch_dense(a, c.wt, NT, p.CPW, grid, p.smem, c.stream);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no kernel instance for this configuration");
   if (rc) return cuda_fail("dense GEMV launch");

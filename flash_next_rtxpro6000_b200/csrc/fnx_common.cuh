@@ -370,23 +370,24 @@ __device__ __forceinline__ uint4 ldg_cg_u4(const void* p) {
   return v;
 }
 
-// The two-pass fp16 staging of the columns [kb, ke) of activation rows (multiples of 8)
-// from produced 16-byte units.  Work item idx is row r = idx / ((ke - kb) / 8) and unit
+// The two-pass fp16 staging of the columns [kb, ke) of activation rows (multiples of 8;
+// shared memory holds exactly that range, row stride stage_row_bytes(ke - kb)) from
+// produced 16-byte units.  Work item idx is row r = idx / ((ke - kb) / 8) and unit
 // u = kb / 8 + idx % ((ke - kb) / 8); unit(in, r, u) returns its 8 bf16 values (zeros
 // when in is false, past the last item).  Every lane of a warp calls it together, on 32
 // consecutive items starting at a multiple of 32, so it may use warp shuffles.  Pass 1
 // finds each row's max |value| over the range, pass 2 converts with the row's power of
-// two (fp16) into the full-K row layout; unscale[r] receives the inverse power of two
+// two (fp16); unscale[r] receives the inverse power of two
 // that the epilogue applies, or 0 where has_row(r) is false.  Threads t0 .. t0 + nth - 1
 // (whole warps) take part and synchronise on named barrier bar_id; unscale[] has room for
 // 2 x 16 words: [16, 32) collects the row maxima as float bits (non-negative floats
 // order like their bits).
 template <int WT, typename RowFn, typename UnitFn>
-__device__ __forceinline__ void stage_units_f16(uint8_t* xs, float* unscale, int nrows, int K,
-                                                int kb, int ke, RowFn has_row, UnitFn unit,
-                                                int t0, int nth, int bar_id) {
+__device__ __forceinline__ void stage_units_f16(uint8_t* xs, float* unscale, int nrows, int kb,
+                                                int ke, RowFn has_row, UnitFn unit, int t0,
+                                                int nth, int bar_id) {
   const int tid = threadIdx.x - t0, lane = threadIdx.x & 31;
-  const int srow = stage_row_bytes(K);
+  const int srow = stage_row_bytes(ke - kb);
   const int upr = (ke - kb) >> 3, u0 = kb >> 3;
   const int total = nrows * upr;
   unsigned* smax = reinterpret_cast<unsigned*>(unscale + 16);
@@ -430,7 +431,7 @@ __device__ __forceinline__ void stage_units_f16(uint8_t* xs, float* unscale, int
   group_sync(bar_id, nth);
   auto put = [&](int idx, const uint4 v) {
     if (idx >= total) return;
-    const int r = idx / upr, u = u0 + idx - r * upr;
+    const int r = idx / upr, u = idx - r * upr;
     const int e = stage_exponent(__uint_as_float(smax[r]));
     *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) =
         bf16x8_to_f16x8_scaled(v, e);
@@ -450,43 +451,42 @@ __device__ __forceinline__ void stage_units_f16(uint8_t* xs, float* unscale, int
 
 // The bf16 form (bf16 weights): the units are copied unchanged, unscale[r] = 1 (or 0).
 template <int WT, typename RowFn, typename UnitFn>
-__device__ __forceinline__ void stage_units_bf16(uint8_t* xs, float* unscale, int nrows, int K,
-                                                 int kb, int ke, RowFn has_row, UnitFn unit,
-                                                 int t0, int nth) {
+__device__ __forceinline__ void stage_units_bf16(uint8_t* xs, float* unscale, int nrows, int kb,
+                                                 int ke, RowFn has_row, UnitFn unit, int t0,
+                                                 int nth) {
   const int tid = threadIdx.x - t0, lane = threadIdx.x & 31;
-  const int srow = stage_row_bytes(K);
+  const int srow = stage_row_bytes(ke - kb);
   const int upr = (ke - kb) >> 3, u0 = kb >> 3;
   const int total = nrows * upr;
   for (int b = tid - lane; b < total; b += nth) {  // warp-uniform: unit() may shuffle
     const int idx = b + lane;
     const bool in = idx < total;
     const int r = in ? idx / upr : 0;
-    const int u = u0 + (in ? idx - r * upr : 0);
-    const uint4 v = unit(in, r, u);
+    const int u = in ? idx - r * upr : 0;
+    const uint4 v = unit(in, r, u0 + u);
     if (in) *reinterpret_cast<uint4*>(xs + (size_t)r * srow + stage_unit_offset<WT>(8 * u)) = v;
   }
   for (int r = tid; r < nrows; r += nth) unscale[r] = has_row(r) ? 1.f : 0.f;
 }
 
-// Stage the columns [kb, ke) of `nrows` activation rows of K bf16 into shared memory in
-// the fragment order above.  Row r is read from src(r) (a bf16 pointer, or nullptr for a
+// Stage the columns [kb, ke) of `nrows` activation rows of bf16 into shared memory in
+// the fragment order above (column kb first).  Row r is read from src(r) (a bf16 pointer, or nullptr for a
 // row that is never used): converted to fp16 with the row's power of two
 // (stage_units_f16), or copied unchanged (bf16 weights).  Reads use ld.global.cg: the
 // rows may have been written by the previous kernel of a programmatic-dependent pair.
 // Callers synchronise the participating threads (named barrier bar_id) after the call.
 template <int WT, typename SrcFn>
-__device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int K,
-                                           int kb, int ke, SrcFn src, int t0, int nth,
-                                           int bar_id) {
+__device__ __forceinline__ void stage_rows(uint8_t* xs, float* unscale, int nrows, int kb,
+                                           int ke, SrcFn src, int t0, int nth, int bar_id) {
   auto has_row = [&](int r) { return src(r) != nullptr; };
   auto unit = [&](bool in, int r, int u) -> uint4 {
     const __nv_bfloat16* p = in ? src(r) : nullptr;
     return p ? ldg_cg_u4(p + 8 * u) : make_uint4(0u, 0u, 0u, 0u);
   };
   if constexpr (WT == W_BF16)
-    stage_units_bf16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth);
+    stage_units_bf16<WT>(xs, unscale, nrows, kb, ke, has_row, unit, t0, nth);
   else
-    stage_units_f16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth, bar_id);
+    stage_units_f16<WT>(xs, unscale, nrows, kb, ke, has_row, unit, t0, nth, bar_id);
 }
 
 // Gated RMSNorm folded into the activation load (the prologue of w8a16_gemv_norm_gated,
@@ -560,7 +560,7 @@ __device__ __forceinline__ uint4 norm_gated_unit(const uint4 xv, const uint4 zv,
 // ke are multiples of the group size.
 template <int WT>
 __device__ __forceinline__ void stage_rows_norm_gated(uint8_t* xs, float* unscale, int nrows,
-                                                      int K, int kb, int ke,
+                                                      int kb, int ke,
                                                       const __nv_bfloat16* x, int64_t ldx,
                                                       const NormGate& ng, int t0, int nth,
                                                       int bar_id) {
@@ -572,9 +572,9 @@ __device__ __forceinline__ void stage_rows_norm_gated(uint8_t* xs, float* unscal
     return norm_gated_unit(xv, zv, 8 * u, ng);
   };
   if constexpr (WT == W_BF16)
-    stage_units_bf16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth);
+    stage_units_bf16<WT>(xs, unscale, nrows, kb, ke, has_row, unit, t0, nth);
   else
-    stage_units_f16<WT>(xs, unscale, nrows, K, kb, ke, has_row, unit, t0, nth, bar_id);
+    stage_units_f16<WT>(xs, unscale, nrows, kb, ke, has_row, unit, t0, nth, bar_id);
 }
 
 // ------------------------------------------------------------------------------------

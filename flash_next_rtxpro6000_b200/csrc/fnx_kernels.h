@@ -48,7 +48,10 @@ struct DenseArgs {
   int tile_groups;        // ceil(row_tiles / RT)
   int n_units;            // tile_groups * ksplit
   int pdl;
-  NormGate norm;          // gated RMSNorm on the activation load (norm.G > 0), else off
+  int xslice;             // 1: gridDim.x % ksplit == 0, so each CTA stages (and sizes)
+                          // only its k split of the activations
+  NormGate norm;          // gated RMSNorm on the activation load (norm.G > 0), else off;
+                          // with xslice the unit k extent is a multiple of norm.G
 };
 
 // One stage of the dense weight ring: RT tiles of weights, then the unit's row scales
@@ -218,6 +221,14 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   return L;
 }
 
+// Compiled forms of the dense kernel: whole activation rows staged; each CTA staging
+// only its k split (xslice); the fused gated RMSNorm (xslice or not, at run time).
+enum DenseMode : int { DENSE_PLAIN = 0, DENSE_SLICE = 1, DENSE_NORM = 2 };
+
+inline int dense_mode(const DenseArgs& a) {
+  return a.norm.G > 0 ? DENSE_NORM : (a.xslice ? DENSE_SLICE : DENSE_PLAIN);
+}
+
 int launch_dense(const DenseArgs& a, int wtype, int nt, int cpw, int grid, size_t smem,
                  cudaStream_t stream);
 int launch_moe_up(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream);
@@ -226,7 +237,7 @@ int launch_moe_sum(const MoeArgs& a, cudaStream_t stream);
 int launch_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
                          cudaStream_t stream);
 
-int dense_occupancy(int wtype, int nt, int cpw, int threads, size_t smem);
+int dense_occupancy(int wtype, int nt, int cpw, int mode, int threads, size_t smem);
 int moe_up_occupancy(int nt, int cpw, int threads, size_t smem);
 int moe_down_occupancy(int nt, int cpw, int threads, size_t smem);
 

@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs 
   }
   // The other warps stage the activations meanwhile; the producer never waits for them.
   if (warp > 0) {
-    stage_rows<W_NVFP4>(xs, unscale, M, H, 0, H, [&](int r) {
+    stage_rows<W_NVFP4>(xs, unscale, M, 0, H, [&](int r) {
       return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
     }, 32, blockDim.x - 32, 1);
     group_sync(1, blockDim.x - 32);

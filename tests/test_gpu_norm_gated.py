@@ -148,3 +148,18 @@ def test_unsupported_group_and_bad_arguments():
         fx.w8a16_gemv_norm_gated(x, w, s, z[:, :128], nw, 96, 1e-6)
     with pytest.raises(ValueError):
         fx.w8a16_gemv_norm_gated(x, w, s, z, nw[:64], 96, 1e-6)
+
+
+@pytest.mark.parametrize("G", [128, 256])
+def test_split_k_slice_staging_and_full_row_fallback(G):
+    # 16 k splits of 128 columns: with G = 128 each CTA stages (and normalises) only its
+    # split; with G = 256 a group would straddle two splits, so full rows are staged.
+    # A grid that is not a multiple of the splits also falls back to full rows.
+    fx = _fx()
+    M, N, K = 4, 640, 2048
+    x, z, nw, w, s, w_np = _case(N, K, M, G, "fp8", seed=G)
+    d = dev()
+    args = (x.to(d), w.to(d), s.to(d), z.to(d), nw.to(d), G, 1e-6)
+    ref = _oracle(x, z, nw, G, w_np, "fp8", s, False)
+    for cfg in ((2, 1, 1, 16), (2, 1, 1, 16, 37), (2, 1, 1, 16, 48)):
+        _check(to_np(fx.w8a16_gemv_norm_gated(*args, cfg=fx.GemvConfig(*cfg))), ref)

@@ -121,6 +121,22 @@ def test_split_k_configs_agree(M):
     assert int(ws.counters.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("M", [1, 9])
+def test_split_k_grids_agree_bitwise(M):
+    # With a grid that is a multiple of ksplit each CTA stages only its k split of x and
+    # publishes its split sums already unscaled; any other grid stages whole rows.  The
+    # power-of-two unscale is exact, so every grid gives the same bits.
+    fx = _fx()
+    N, K = 1280, 2048
+    x, w, s, w_np = _case(N, K, M, "int8", torch.float32, seed=77)
+    x, w, s = x.to(dev()), w.to(dev()), s.to(dev())
+    outs = [fx.w8a16_gemv(x, w, s, cfg=fx.GemvConfig(8, 1, 1, 4, grid)) for grid in (0, 40, 37, 3)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    ref = ow8.gemv(x.float().cpu().numpy(), w_np, "int8", s.cpu().numpy())
+    assert rel_err(to_np(outs[0]), ref) <= REL_TOL
+
+
 @pytest.mark.parametrize("M", [1, 4, 16])
 def test_graph_replay_bitwise_and_counters_reset(M):
     # verify_v3.py:46-83
