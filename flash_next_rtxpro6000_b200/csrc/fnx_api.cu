@@ -150,6 +150,33 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
     return finish_plan(M, K, NT, p);
   }
   const int sms = fnx::num_sms();
+  // Mid-size problems (fewer than 8 row tiles per SM) are latency-bound.  Measured on
+  // B200 over 1024..16384 rows x 2048..8192 columns (int8, fp8, NVFP4; M = 1, 4, 16),
+  // the best tilings take one row tile per unit, the fewest k splits that keep a unit
+  // within nu_max chunks (the staged activations and a deep ring must fit; a split-K
+  // fix-up costs more than a longer unit), and about 8 consumer warps at M = 1, 16 above.
+  if ((int64_t)p.row_tiles < 8LL * sms) {
+    const int nu_max = M <= 1 ? 96 : (M <= 8 ? 64 : 32);
+    const int wt = M <= 1 ? 8 : 16;
+    for (int k = 1; k <= nch && k <= sms; ++k) {
+      if (nch % k || nch / k > nu_max) continue;
+      const int nu = nch / k;
+      int cpw = 1;
+      while (cpw < 8 && nu % (2 * cpw) == 0 && nu / cpw > wt) cpw *= 2;
+      if (nu / cpw > 16) continue;
+      DensePlan q = p;
+      q.ksplit = k;
+      q.nch_u = nu;
+      q.W = nu / cpw;
+      q.CPW = cpw;
+      q.RT = 1;
+      q.xslice = k > 1 ? 1 : 0;
+      if (layout_plan(M, K, NT, q)) {
+        p = q;
+        return FNX_OK;
+      }
+    }
+  }
   // Search (k split, row tiles per unit RT, chunks per consumer warp CPW) with a cost
   // model of one CTA's time: rounds of units x the unit's chunk rows, plus a per-unit
   // overhead of each consumer warp (about 1.5 chunks) and of the split-K fix-up; fewer
