@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
   uint64_t* empty = full + NS;
   uint64_t* rfull = empty + NS;
   uint64_t* rfree = rfull + RS;
+  uint64_t* xbar = rfree + RS;  // bulk copy of the activation rows
   uint8_t* stages = smem + L.stages;
   uint8_t* xs = smem + L.xs;
   float* unscale = reinterpret_cast<float*>(smem + L.unscale);
@@ -92,6 +93,7 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
       mbar_init(&rfull[r], W);
       mbar_init(&rfree[r], 1);
     }
+    mbar_init(xbar, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -166,30 +168,29 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
     cp_async_arrive(&full[s]);
   };
 
+  // xslice: the grid is a multiple of ksplit, so every unit of this CTA has the k split
+  // first % ksplit and only that k range of the activations is staged (and sized).
+  const int kb = xslice ? (first % ksplit) * kpu : 0;
+  const int ke = xslice ? kb + kpu : K;
+  const __nv_bfloat16* xrows = reinterpret_cast<const __nv_bfloat16*>(a.x);
+  const bool x_direct = M <= 2;  // rows loaded by the staging warps, no bulk copy
   UnitCursor pc;  // producer position
   pc.init(first, stride, ksplit, NS);
   if (warp == 0) {
+    // The weights and scales do not depend on the previous kernel; the activations may.
+    // Without programmatic dependent launch the activation rows go first, so that they do
+    // not queue behind the weight stages in the copy engine.
+    if (lane == 0 && !a.pdl && !x_direct) issue_x_rows(xs, M, kb, ke, xrows, a.ldx, xbar);
     const int pre = my_units < NS ? my_units : NS;
     for (int i = 0; i < pre; ++i, pc.next()) issue(pc);
   }
-  // The weights and scales do not depend on the previous kernel; the activations may.
   pdl_wait();
+  if (tid == 0 && a.pdl && !x_direct) issue_x_rows(xs, M, kb, ke, xrows, a.ldx, xbar);
   // The other warps stage the activations meanwhile; the producer never waits for them.
   if (warp > 0) {
-    // xslice: the grid is a multiple of ksplit, so every unit of this CTA has the k split
-    // first % ksplit and only that k range of the activations is staged (and sized).
-    const int kb = xslice ? (first % ksplit) * kpu : 0;
-    const int ke = xslice ? kb + kpu : K;
-    if constexpr (MODE == DENSE_NORM && WT != W_NVFP4) {
-      // kb and ke are multiples of the norm group (the host checks)
-      stage_rows_norm_gated<WT>(xs, unscale, M, kb, ke,
-                                reinterpret_cast<const __nv_bfloat16*>(a.x), a.ldx, a.norm, 32,
-                                blockDim.x - 32, 1);
-    } else {
-      stage_rows<WT>(xs, unscale, M, kb, ke, [&](int r) {
-        return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
-      }, 32, blockDim.x - 32, 1);
-    }
+    constexpr bool kNorm = MODE == DENSE_NORM && WT != W_NVFP4;
+    stage_rows_bulk<WT, kNorm>(xs, unscale, M, kb, ke, xrows, a.ldx, a.norm, xbar, a.err,
+                               x_direct, 32, blockDim.x - 32, 1);
     group_sync(1, blockDim.x - 32);
   }
 

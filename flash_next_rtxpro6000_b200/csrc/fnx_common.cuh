@@ -83,6 +83,12 @@ __device__ __forceinline__ uint32_t ldg_u16_stream(const void* p, uint64_t pol) 
   return (uint32_t)v;
 }
 
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -556,27 +562,6 @@ __device__ __forceinline__ uint4 norm_gated_unit(const uint4 xv, const uint4 zv,
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
-// stage_rows for the first nrows rows of x, normalised and gated on the way in; kb and
-// ke are multiples of the group size.
-template <int WT>
-__device__ __forceinline__ void stage_rows_norm_gated(uint8_t* xs, float* unscale, int nrows,
-                                                      int kb, int ke,
-                                                      const __nv_bfloat16* x, int64_t ldx,
-                                                      const NormGate& ng, int t0, int nth,
-                                                      int bar_id) {
-  auto has_row = [](int) { return true; };
-  auto unit = [&](bool in, int r, int u) -> uint4 {
-    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-    const uint4 xv = in ? ldg_cg_u4(x + (size_t)r * ldx + 8 * u) : zero;
-    const uint4 zv = in ? ldg_cg_u4(ng.z + (size_t)r * ng.ldz + 8 * u) : zero;
-    return norm_gated_unit(xv, zv, 8 * u, ng);
-  };
-  if constexpr (WT == W_BF16)
-    stage_units_bf16<WT>(xs, unscale, nrows, kb, ke, has_row, unit, t0, nth);
-  else
-    stage_units_f16<WT>(xs, unscale, nrows, kb, ke, has_row, unit, t0, nth, bar_id);
-}
-
 // ------------------------------------------------------------------------------------
 // Asynchronous pipeline primitives: mbarriers and bulk (TMA) copies into shared memory.
 // Every wait is bounded: after kWaitLimitNs of polling it reports failure, and the
@@ -585,7 +570,7 @@ __device__ __forceinline__ void stage_rows_norm_gated(uint8_t* xs, float* unscal
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 enum ErrCode : int { ERR_NONE = 0, ERR_WAIT_FULL = 1, ERR_WAIT_EMPTY = 2, ERR_WAIT_RED = 3,
-                     ERR_WAIT_RFREE = 4, ERR_DRAIN = 5 };
+                     ERR_WAIT_RFREE = 4, ERR_DRAIN = 5, ERR_WAIT_X = 6 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -758,6 +743,111 @@ __device__ __forceinline__ int phys_lo(int g) { return (g & 1) ? g + 8 : g; }
 __device__ __forceinline__ int phys_hi(int g) { return (g & 1) ? g : g + 8; }
 __device__ __forceinline__ int tile_row_offset(int r, int ub) {
   return r < 8 ? r * ub : tile_half_offset(ub) + (r - 8) * ub;
+}
+
+// Stage the columns [kb, ke) of the first nrows activation rows like stage_rows, with
+// the rows brought in by the bulk-copy engine: issue_x_rows (called once, by one thread
+// of the CTA, before or during this call) copies each raw bf16 row into its own
+// shared-memory slot, completing on xbar (phase 0), so the whole block arrives after one
+// memory latency.  With `direct` (one or two rows, where the copy engine's latency is
+// not repaid) no copy is issued and pass 1 loads the units from global memory itself.  The participating warps then split the
+// rows into segments of whole 32-unit batches (several warps per row when there are few
+// rows) and, with no division in the loops:
+//   pass 1: each lane keeps a running max |value| over its units (with the fused norm,
+//           NORM, it first replaces each unit by its normalised, gated bf16 value,
+//           z read from global memory); one warp reduction and one shared atomic per
+//           segment give the row maxima;
+//   pass 2: each unit is converted to fp16 with its row's power of two and moved to its
+//           fragment slot (a permutation inside its weight chunk: a warp reads its 32
+//           units, which cover whole chunks, before writing them back).
+// x rows, ldx and kb keep 16-byte alignment; with the norm, kb and ke are multiples of
+// the group.  An expired wait records ERR_WAIT_X and stages nothing further.
+// The bulk copies of stage_rows_bulk, issued by one thread: the raw bf16 columns
+// [kb, ke) of rows 0 .. nrows - 1 into their shared-memory row slots, completing on xbar.
+__device__ __forceinline__ void issue_x_rows(uint8_t* xs, int nrows, int kb, int ke,
+                                             const __nv_bfloat16* x, int64_t ldx, uint64_t* xbar) {
+  const int kx = ke - kb;
+  const int srow = stage_row_bytes(kx);
+  mbar_arrive_expect_tx(xbar, (uint32_t)(nrows * kx * 2));
+  const uint64_t pol = policy_evict_last();  // every CTA reads the same rows
+  for (int r = 0; r < nrows; ++r)
+    bulk_g2s(xs + (size_t)r * srow, x + (size_t)r * ldx + kb, (uint32_t)(kx * 2), xbar, pol);
+}
+
+template <int WT, bool NORM>
+__device__ __forceinline__ void stage_rows_bulk(uint8_t* xs, float* unscale, int nrows, int kb,
+                                                int ke, const __nv_bfloat16* x, int64_t ldx,
+                                                const NormGate ng, uint64_t* xbar, int* err,
+                                                bool direct, int t0, int nth, int bar_id) {
+  const int tid = threadIdx.x - t0, lane = threadIdx.x & 31;
+  const int kx = ke - kb;
+  const int srow = stage_row_bytes(kx);
+  const int upr = kx >> 3;                      // 16-byte units per row
+  const int nwarps = nth >> 5, w = tid >> 5;
+  const int segs = max(1, min(nwarps / nrows, (upr + 31) >> 5));  // warps per row
+  const int seg_len = ((upr + segs - 1) / segs + 31) & ~31;         // units, whole batches
+  const int tasks = nrows * segs;
+  unsigned* smax = reinterpret_cast<unsigned*>(unscale + 16);
+  for (int r = tid; r < nrows; r += nth) smax[r] = 0u;
+  group_sync(bar_id, nth);
+  if (!direct && !mbar_wait(xbar, 0)) {
+    record_error(err, ERR_WAIT_X);
+    return;
+  }
+  if constexpr (WT == W_BF16 && !NORM) {  // the raw rows are the fragment layout already
+    if (direct)
+      for (int i = tid; i < nrows * upr; i += nth) {
+        const int r = i / upr, u = i - r * upr;
+        *reinterpret_cast<uint4*>(xs + (size_t)r * srow + u * 16) =
+            ldg_cg_u4(x + (size_t)r * ldx + kb + 8 * u);
+      }
+    for (int r = tid; r < nrows; r += nth) unscale[r] = 1.f;
+  } else {
+    for (int task = w; task < tasks; task += nwarps) {  // pass 1
+      const int r = task / segs, sg = task - r * segs;
+      const int u0 = sg * seg_len, u1 = min(upr, u0 + seg_len);
+      uint8_t* row = xs + (size_t)r * srow;
+      float m = 0.f;
+      for (int b = u0; b < u1; b += 32) {  // warp-uniform
+        const int u = b + lane;
+        const bool in = u < u1;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (in) v = direct ? ldg_cg_u4(x + (size_t)r * ldx + kb + 8 * u) : lds128(row + u * 16);
+        if constexpr (NORM) {
+          const uint4 zv = in ? ldg_cg_u4(ng.z + (size_t)r * ng.ldz + kb + 8 * u)
+                              : make_uint4(0u, 0u, 0u, 0u);
+          v = norm_gated_unit(v, zv, kb + 8 * u, ng);
+        }
+        if (in && (NORM || direct)) *reinterpret_cast<uint4*>(row + u * 16) = v;
+        if (in) m = fmaxf(m, bf16x8_absmax(v));
+      }
+      unsigned bits = __float_as_uint(m);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+      if (lane == 0 && u0 < u1) atomicMax(&smax[r], bits);
+    }
+    group_sync(bar_id, nth);
+    if constexpr (WT == W_BF16) {  // normalised rows, already in the fragment layout
+      for (int r = tid; r < nrows; r += nth) unscale[r] = 1.f;
+    } else {
+      for (int task = w; task < tasks; task += nwarps) {  // pass 2
+        const int r = task / segs, sg = task - r * segs;
+        const int u0 = sg * seg_len, u1 = min(upr, u0 + seg_len);
+        uint8_t* row = xs + (size_t)r * srow;
+        const int e = stage_exponent(__uint_as_float(smax[r]));
+        for (int b = u0; b < u1; b += 32) {  // warp-uniform
+          const int u = b + lane;
+          const bool in = u < u1;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (in) v = bf16x8_to_f16x8_scaled(lds128(row + u * 16), e);
+          __syncwarp();  // every lane has read its raw unit before any lane overwrites a chunk
+          if (in) *reinterpret_cast<uint4*>(row + stage_unit_offset<WT>(8 * u)) = v;
+        }
+      }
+      for (int r = tid; r < nrows; r += nth)
+        unscale[r] = pow2f(-stage_exponent(__uint_as_float(smax[r])));
+    }
+  }
 }
 
 }  // namespace fnx

@@ -82,7 +82,7 @@ __host__ __device__ inline DenseLayout dense_layout(int M, int K, int W, int NS,
   DenseLayout L;
   int off = 0;
   L.bars = off;
-  off = dense_align(off + (2 * NS + 2 * RS) * 8, 128);
+  off = dense_align(off + (2 * NS + 2 * RS + 1) * 8, 128);  // + the activation barrier
   L.stages = off;
   off += NS * stage_bytes;
   L.xs = dense_align(off, 128);
