@@ -6,7 +6,8 @@ M = 1, 4 and 16 tokens.  The weights (311 MB) exceed the 126 MB L2, so every cal
 streams them from HBM.  Metric: HBM GB/s of algorithmic bytes (weights + scales +
 activations + logits + argmax), whole-job aggregate; µs per call is reported beside it.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lm_head|draft_head|nvfp4|moe]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated]
     python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
 
 With N > 1 (torchrun, one rank per GPU, NCCL) the lm_head is vocab-sharded: each rank
@@ -32,6 +33,7 @@ if ROOT not in sys.path:
 METRIC = "µs/call and HBM GB/s (% of ~8 TB/s) for NVFP4 MoE & W8A16 GEMV at M=1–16"
 UNIT = "GB/s"
 FALLBACK_HBM = 6650.0
+L2_BYTES = 126 * 1024 * 1024
 
 
 def parse_args():
@@ -40,7 +42,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["lm_head", "draft_head", "nvfp4", "moe"],
+    ap.add_argument("--workload", choices=["lm_head", "draft_head", "nvfp4", "moe", "norm_gated"],
                     default="lm_head")
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -223,6 +225,8 @@ def main():
         res = bench_lm_head(args, fx, syn, dev, rank, world)
     elif args.workload == "nvfp4":
         res = bench_nvfp4(args, fx, syn, dev)
+    elif args.workload == "norm_gated":
+        res = bench_norm_gated(args, fx, syn, dev)
     else:
         res = bench_moe(args, fx, syn, dev)
     if world > 1:
@@ -291,6 +295,11 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
     r0 = rank * shard
     w = head.w[r0:r0 + shard].contiguous().to(dev)
     s = head.scale[r0:r0 + shard].contiguous().to(dev)
+    # weight copies rotated call by call so that at least 2x L2 of weights lie between
+    # two reads of one copy (the draft head, 100 MB, and vocab shards fit in L2 alone)
+    copies = max(1, -(-2 * L2_BYTES // (shard * K)))
+    wl = [w] + [w.clone() for _ in range(copies - 1)]
+    rot = [0]
     xs = [syn.activations(m, seed=1).to(dev) for m in Ms]
     ys = [torch.empty(m, shard, dtype=torch.bfloat16, device=dev) for m in Ms]
     ams = [torch.empty(m, dtype=torch.int64, device=dev) for m in Ms]
@@ -306,8 +315,10 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
 
     def call(i, x):
         # the operator API's C call, with the raw key output for the sharded reduction
+        wc = wl[rot[0] % copies]
+        rot[0] += 1
         rc = lib.fnx_w8a16_gemv(
-            x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), _lib.W_INT8, s.data_ptr(),
+            x.data_ptr(), x.stride(0), wc.data_ptr(), wc.stride(0), _lib.W_INT8, s.data_ptr(),
             _lib.SCALE_BF16_ROW, ys[i].data_ptr(), ys[i].stride(0), None, 0, 0, 0,
             ams[i].data_ptr() if world == 1 else None,
             keys[i].data_ptr() if world > 1 else None, r0, x.shape[0], shard, K, None,
@@ -348,7 +359,10 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8/bf16 (fp32 accumulate)", "data": "synthetic",
         "config": {"workload": f"w8a16_{args.workload}_{V}x{K}_argmax", "M": Ms,
-                   "weights": "int8 per-row bf16 scale", "l2": "weights 311 MB > 126 MB L2, no flush needed",
+                   "weights": "int8 per-row bf16 scale",
+                   "l2": f"{copies} weight cop{'y' if copies == 1 else 'ies'} of "
+                         f"{shard * K / 1e6:.0f} MB rotated per call (>= 2x the 126 MB L2 "
+                         "between reads of one copy), no flush",
                    "parallelism": f"vocab-sharded x{world} + NCCL MAX all-reduce of argmax keys"
                    if world > 1 else "single GPU"},
         "us_per_call": {str(m): round(v, 3) for m, v in per_m.items()},
@@ -359,7 +373,7 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
         "gpu_launches": args.steps * len(Ms) * (2 if world > 1 else 1),
     }
     if not args.no_e2e:
-        res["e2e"] = e2e_lm_head(args, fx, syn, dev, w, s, Ms, world, rank, r0, shard, V, K)
+        res["e2e"] = e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
 
@@ -379,7 +393,7 @@ def _lib_handle():
     return _lib.lib()
 
 
-def e2e_lm_head(args, fx, syn, dev, w, s, Ms, world, rank, r0, shard, V, K):
+def e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K):
     """Public API end to end: pinned host x -> device, w8a16_gemv(argmax_out=...),
     argmax -> pinned host, one host sync per step."""
     import torch
@@ -392,8 +406,12 @@ def e2e_lm_head(args, fx, syn, dev, w, s, Ms, world, rank, r0, shard, V, K):
     ys = [torch.empty(m, shard, dtype=torch.bfloat16, device=dev) for m in Ms]
     from flash_next_rtxpro6000_b200 import sharded
 
+    rot = [0]
+
     def step():
         for i, m in enumerate(Ms):
+            w = wl[rot[0] % len(wl)]  # rotated like the device-timed calls
+            rot[0] += 1
             dx[i].copy_(hx[i], non_blocking=True)
             if world == 1:
                 fx.w8a16_gemv(dx[i], w, s, out=ys[i], argmax_out=dam[i], pdl=True)
@@ -466,6 +484,58 @@ def bench_nvfp4(args, fx, syn, dev):
             "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": "nvfp4_gemv_4096x2048", "M": Ms,
                        "l2": f"{copies} weight copies rotated in one CUDA graph (> 4x L2)"},
+            "per_m": per_m,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": None}
+
+
+def bench_norm_gated(args, fx, syn, dev):
+    """The fused gated-RMSNorm GEMV at the reference's out_proj shape
+    (kernels/microbench/h1/h1_check.py:21-27: N = 2560, K = 48 x 128, group 128, fp8
+    weights with fp32 per-row scales, sigmoid gate): 12 weight copies rotated (> L2)
+    inside one CUDA graph.  `plain_gemv_us` is the same GEMV without the norm."""
+    import torch
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    N, K, G, copies = 2560, 48 * 128, 128, 12
+    gen = torch.Generator().manual_seed(0)
+    ws = [((torch.randn(N, K, generator=gen) * 64).to(torch.float8_e4m3fn)).to(dev)
+          for _ in range(copies)]
+    s = (torch.rand(N, generator=gen) / 448).to(dev)
+    nw = (torch.randn(G, generator=gen) * 0.3 + 1.0).bfloat16().to(dev)
+    peak, src = measured_peak()
+    per_m, total_bytes, total_ms = {}, 0, 0.0
+    sampler = ClockSampler(_gpu_id(dev))
+    clocks = None
+    for M in Ms:
+        x = (torch.randn(M, K, generator=gen) * 0.5).bfloat16().to(dev)
+        z = (torch.randn(M, K, generator=gen) * 0.5).bfloat16().to(dev)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        reps = max(3, args.steps // copies)
+        res = {}
+        for name, fn in (("norm", lambda w: fx.w8a16_gemv_norm_gated(
+                              x, w, s, z, nw, G, 1e-6, sigmoid_gate=True, out=y)),
+                         ("plain", lambda w: fx.w8a16_gemv(x, w, s, out=y))):
+            g = _graph_of([(lambda w=w: fn(w)) for w in ws])
+            ms, ck = _timed(g.replay, reps, max(3, args.warmup // copies), dev, 1,
+                            sampler if (M == Ms[-1] and name == "norm") else None)
+            clocks = ck or clocks
+            res[name] = (ms, ms / (reps * copies) * 1e3)
+            del g
+        b = N * K + 4 * N + 2 * G + 4 * M * K + 2 * M * N
+        us = res["norm"][1]
+        per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1),
+                         "plain_gemv_us": round(res["plain"][1], 3)}
+        total_bytes += b * reps * copies
+        total_ms += res["norm"][0]
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8/bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": "w8a16_norm_gated_2560x6144_g128", "M": Ms,
+                       "l2": f"{copies} weight copies rotated in one CUDA graph (> L2)"},
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},

@@ -553,7 +553,7 @@ __device__ __forceinline__ uint4 norm_gated_unit(const uint4 xv, const uint4 zv,
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const float z = zf[2 * i + h];
-      const float sg = 1.f / (1.f + expf(-z));
+      const float sg = __fdividef(1.f, 1.f + __expf(-z));  // 0 where exp overflows
       y[h] = xf[2 * i + h] * rstd * nw[2 * i + h] * (ng.sigmoid ? sg : z * sg);
     }
     const __nv_bfloat162 b = __floats2bfloat162_rn(y[0], y[1]);
@@ -808,18 +808,25 @@ __device__ __forceinline__ void stage_rows_bulk(uint8_t* xs, float* unscale, int
       const int u0 = sg * seg_len, u1 = min(upr, u0 + seg_len);
       uint8_t* row = xs + (size_t)r * srow;
       float m = 0.f;
-      for (int b = u0; b < u1; b += 32) {  // warp-uniform
-        const int u = b + lane;
-        const bool in = u < u1;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (in) v = direct ? ldg_cg_u4(x + (size_t)r * ldx + kb + 8 * u) : lds128(row + u * 16);
-        if constexpr (NORM) {
-          const uint4 zv = in ? ldg_cg_u4(ng.z + (size_t)r * ng.ldz + kb + 8 * u)
-                              : make_uint4(0u, 0u, 0u, 0u);
-          v = norm_gated_unit(v, zv, kb + 8 * u, ng);
+      for (int b = u0; b < u1; b += 64) {  // two batches per step, warp-uniform
+        uint4 v[2], zv[2];
+        bool in[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // all loads of the step first
+          const int u = b + 32 * h + lane;
+          in[h] = u < u1;
+          v[h] = zv[h] = make_uint4(0u, 0u, 0u, 0u);
+          if (in[h]) v[h] = direct ? ldg_cg_u4(x + (size_t)r * ldx + kb + 8 * u) : lds128(row + u * 16);
+          if constexpr (NORM)
+            if (in[h]) zv[h] = ldg_cg_u4(ng.z + (size_t)r * ng.ldz + kb + 8 * u);
         }
-        if (in && (NORM || direct)) *reinterpret_cast<uint4*>(row + u * 16) = v;
-        if (in) m = fmaxf(m, bf16x8_absmax(v));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int u = b + 32 * h + lane;
+          if constexpr (NORM) v[h] = norm_gated_unit(v[h], zv[h], kb + 8 * u, ng);
+          if (in[h] && (NORM || direct)) *reinterpret_cast<uint4*>(row + u * 16) = v[h];
+          if (in[h]) m = fmaxf(m, bf16x8_absmax(v[h]));
+        }
       }
       unsigned bits = __float_as_uint(m);
 #pragma unroll
