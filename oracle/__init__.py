@@ -9,7 +9,8 @@ path and its NVFP4 codec, so the CUDA kernels can be checked against it:
 * ``oracle.w8a16``    -- the W8A16 GEMV (int8 / fp8 weights, per-row scales), its fused
   gate_up SiLU form and the greedy argmax;
 * ``oracle.moe``      -- the routed-MoE layer (server and checkpoint row orders), with an
-  optional always-on shared expert.
+  optional always-on shared expert;
+* ``oracle.router``   -- the router projection and the softmax top-k routing table.
 
 Parity pins: the functions are checked against golden vectors produced by the
 reference's own Python code (``tests/golden/make_golden.py``, fixtures in
@@ -20,4 +21,4 @@ import this package, and only as the checker or the timed CPU baseline.  The pro
 (``flash_next_rtxpro6000_b200``) never imports it.
 """
 
-from . import moe, numerics, nvfp4, w8a16  # noqa: F401
+from . import moe, numerics, nvfp4, router, w8a16  # noqa: F401

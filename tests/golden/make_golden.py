@@ -16,6 +16,9 @@ It imports the reference's Python modules by file path, with empty stand-ins for
   small seeded layer, checkpoint row order;
 * ``w8a16_norm_gated.npz`` -- the same kernel's fused gated-RMSNorm form
   (w8a16_gemv.py:186-259, SiLU and sigmoid gates) at M=1 and M=4 under the interpreter
+* ``router_topk.npz``   -- the reference's packed-key softmax top-k router (patches
+  0110 + 0111, moe_router_softmax_fast.py) under the interpreter: 512/256/128 experts,
+  top-10/8/6, renormalised or not, exact ties, a NaN and -0.0 logits;
 * ``w8a16_kernel.npz``  -- the reference's Triton W8A16 kernel itself
   (w8a16_gemv.py:642-666) at M=1 under the Triton CPU interpreter, int8 and fp8
   weights, per-row fp32 and bf16 scales, bf16 and fp32 destinations.
@@ -239,6 +242,60 @@ def make_w8a16_interp(ref: Path):
                     str(HERE / "w8a16_kernel.npz")], check=True, env=env, cwd=str(HERE))
 
 
+_INTERP_ROUTER = r'''
+import sys, types, importlib.util, numpy as np, torch
+for n in ("sglang", "sglang.kernels", "sglang.kernels.jit", "sglang.kernels.ops",
+          "sglang.kernels.ops.moe"):
+    m = types.ModuleType(n); m.__path__ = []; sys.modules[n] = m
+u = types.ModuleType("sglang.kernels.jit.utils"); u.is_arch_support_pdl = lambda: False
+sys.modules["sglang.kernels.jit.utils"] = u
+spec = importlib.util.spec_from_file_location("rfast", sys.argv[1])
+rf = importlib.util.module_from_spec(spec); spec.loader.exec_module(rf)
+g = torch.Generator().manual_seed(5)
+out = {}
+cases = {
+    # 512 experts, the served top-10 (renormalised) and a plain top-8
+    "a": ((torch.randn(4, 512, generator=g) * 2).bfloat16(), 10, True),
+    "b": ((torch.randn(3, 512, generator=g) * 2).bfloat16(), 8, False),
+    # coarse values: many exact ties (lowest id must win), fewer experts
+    "c": ((torch.randint(-3, 4, (5, 256), generator=g).float() * 0.5).bfloat16(), 10, True),
+    # a NaN logit and -0.0 entries
+    "d": ((torch.randn(2, 128, generator=g)).bfloat16(), 6, True),
+}
+cases["d"][0][0, 7] = float("nan")
+cases["d"][0][1, 3:9] = -0.0
+for key, (scores, k, renorm) in cases.items():
+    zero = torch.zeros(scores.shape[1], dtype=torch.float32)
+    w, i = rf.route_softmax_fast(scores, zero, k, renorm)
+    out[f"scores_{key}"] = scores.float().numpy()
+    out[f"topk_{key}"] = np.array([k, int(renorm)])
+    out[f"w_{key}"] = w.numpy()
+    out[f"ids_{key}"] = i.numpy()
+np.savez_compressed(sys.argv[2], **out)
+'''
+
+
+def make_router_topk_interp(ref: Path):
+    """The reference's softmax top-k router (patches 0110 + 0111 applied to an empty tree,
+    python/sglang/kernels/ops/moe/moe_router_softmax_fast.py) under the Triton CPU
+    interpreter -> router_topk.npz."""
+    import shutil
+    import tempfile
+
+    tmp = Path(tempfile.mkdtemp())
+    try:
+        subprocess.run(["git", "init", "-q"], cwd=tmp, check=True)
+        rel = "python/sglang/kernels/ops/moe/moe_router_softmax_fast.py"
+        for p in ("0110", "0111"):
+            patch = next((ref / "patches/sglang/series").glob(f"{p}-*.patch"))
+            subprocess.run(["git", "apply", f"--include={rel}", str(patch)], cwd=tmp, check=True)
+        env = dict(os.environ, TRITON_INTERPRET="1", CUDA_VISIBLE_DEVICES="")
+        subprocess.run([sys.executable, "-c", _INTERP_ROUTER, str(tmp / rel),
+                        str(HERE / "router_topk.npz")], check=True, env=env, cwd=str(HERE))
+    finally:
+        shutil.rmtree(tmp)
+
+
 def main():
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FNX_REFERENCE", ""))
     if not (ref / "kernels").is_dir():
@@ -249,6 +306,7 @@ def main():
     make_moe(refs, w4)
     make_w8a16_interp(ref)
     make_w8a16_norm_interp(ref)
+    make_router_topk_interp(ref)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -10,7 +10,7 @@ import os
 import numpy as np
 import pytest
 
-from oracle import moe, numerics, nvfp4, w8a16
+from oracle import moe, numerics, nvfp4, router, w8a16
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -178,3 +178,18 @@ def test_norm_gated_oracle_matches_reference_kernel(M, gate):
     assert np.array_equal(yt, ref)
     y = w8a16.gemv_norm_gated(*args, g["w_int8"], "int8", g["scale_f32"], sigmoid_gate=sig)
     assert np.abs(y - ref).max() / np.abs(ref).max() < 2e-2
+
+
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
+def test_router_topk_oracle_matches_reference_kernel(case):
+    # The reference's packed-key softmax top-k (patches 0110 + 0111) under the Triton CPU
+    # interpreter: ids bit-exact (ties to the lowest id, NaN floored, -0.0 as +0.0),
+    # weights to fp32 rounding (the kernel's exp is ex2.approx-based), NaN rows NaN.
+    g = _npz("router_topk.npz")
+    k, renorm = (int(v) for v in g[f"topk_{case}"])
+    w, ids = router.softmax_topk(g[f"scores_{case}"], k, bool(renorm))
+    assert np.array_equal(ids, g[f"ids_{case}"])
+    ref = g[f"w_{case}"]
+    nan = np.isnan(ref)
+    assert np.array_equal(nan, np.isnan(w))
+    assert np.allclose(w[~nan], ref[~nan], rtol=2e-6, atol=1e-9)
