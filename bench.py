@@ -7,7 +7,7 @@ streams them from HBM.  Metric: HBM GB/s of algorithmic bytes (weights + scales 
 activations + logits + argmax), whole-job aggregate; µs per call is reported beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated]
+                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router]
     python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
 
 With N > 1 (torchrun, one rank per GPU, NCCL) the lm_head is vocab-sharded: each rank
@@ -42,7 +42,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["lm_head", "draft_head", "nvfp4", "moe", "norm_gated"],
+    ap.add_argument("--workload",
+                    choices=["lm_head", "draft_head", "nvfp4", "moe", "norm_gated", "router"],
                     default="lm_head")
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -227,6 +228,8 @@ def main():
         res = bench_nvfp4(args, fx, syn, dev)
     elif args.workload == "norm_gated":
         res = bench_norm_gated(args, fx, syn, dev)
+    elif args.workload == "router":
+        res = bench_router(args, fx, syn, dev)
     else:
         res = bench_moe(args, fx, syn, dev)
     if world > 1:
@@ -536,6 +539,52 @@ def bench_norm_gated(args, fx, syn, dev):
             "dtype": "fp8/bf16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": "w8a16_norm_gated_2560x6144_g128", "M": Ms,
                        "l2": f"{copies} weight copies rotated in one CUDA graph (> L2)"},
+            "per_m": per_m,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": None}
+
+
+def bench_router(args, fx, syn, dev):
+    """The fused MoE router (router GEMV 512 x 2048 bf16 + softmax top-10, renormalised)
+    at the draft MoE's shape: 128 router-weight copies (256 MB, > 2x L2) rotated inside
+    one CUDA graph.  `unfused_us` is router_gemv + route_softmax_fast (two launches)."""
+    import torch
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    E, K, k, copies = syn.EXPERTS, syn.HIDDEN, 10, 128
+    gen = torch.Generator().manual_seed(0)
+    ws = [((torch.randn(E, K, generator=gen) * 0.05).bfloat16()).to(dev) for _ in range(copies)]
+    peak, src = measured_peak()
+    per_m, total_bytes, total_ms = {}, 0, 0.0
+    sampler = ClockSampler(_gpu_id(dev))
+    clocks = None
+    for M in Ms:
+        x = syn.activations(M, seed=1).to(dev)
+        reps = max(3, args.steps // copies)
+        res = {}
+        for name, fn in (("fused", lambda w: fx.router_topk(x, w, None, k, True, pdl=True)),
+                         ("unfused", lambda w: fx.route_softmax_fast(
+                             fx.router_gemv(x, w, pdl=True), None, k, True, pdl=True))):
+            g = _graph_of([(lambda w=w: fn(w)) for w in ws])
+            ms, ck = _timed(g.replay, reps, max(3, args.warmup // copies), dev, 1,
+                            sampler if (M == Ms[-1] and name == "fused") else None)
+            clocks = ck or clocks
+            res[name] = (ms, ms / (reps * copies) * 1e3)
+            del g
+        b = 2 * E * K + 2 * M * K + 4 * M * E + 8 * M * k
+        us = res["fused"][1]
+        per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1),
+                         "unfused_us": round(res["unfused"][1], 3)}
+        total_bytes += b * reps * copies
+        total_ms += res["fused"][0]
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"router_topk_{E}x{K}_top{k}", "M": Ms,
+                       "l2": f"{copies} router-weight copies rotated in one CUDA graph (> 2x L2)"},
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},

@@ -9,6 +9,8 @@ the hand-written CUDA library ``_fnx.so``):
 * ``w4a16_nvfp4_gemv`` -- NVFP4 GEMV; ``quantize_nvfp4`` / ``dequantize_nvfp4`` codec;
 * ``draft_moe_gemv`` / ``moe_gemv`` -- routed NVFP4 MoE expert GEMVs (gate_up + SiLU,
   down + router-weighted route sum), M <= 16;
+* ``router_gemv``, ``route_softmax_fast``, ``router_topk`` -- the MoE router projection
+  and its softmax top-k routing table (fused into one launch by ``router_topk``);
 * ``sharded`` -- vocab-sharded lm_head and expert-sharded MoE over torch.distributed.
 """
 
@@ -40,5 +42,7 @@ from .draft_moe_gemv import (  # noqa: F401
     moe_gemv,
     unsupported_reason,
 )
+
+from .router import covered, route_softmax_fast, router_gemv, router_topk  # noqa: F401
 
 __version__ = "0.1.0"

@@ -25,6 +25,8 @@ EXPORTED = (
     "fnx_w8a16_gemv_static_ws",
     "fnx_w8a16_gemv_silu_mul",
     "fnx_w8a16_gemv_norm_gated",
+    "fnx_router_gemv_topk",
+    "fnx_softmax_topk",
     "fnx_w4a16_nvfp4_gemv",
     "fnx_moe_workspace_bytes",
     "fnx_moe_gemv",
@@ -116,6 +118,11 @@ def _declare(lib):
         _P, c_int64, _P, c_int64, _P, c_int, c_int, c_float, c_int, _P, c_int64, c_int, _P,
         c_int, _P, c_int64, c_int, c_int, c_int, c_int, POINTER(FnxGemvCfg),
         POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_router_gemv_topk.argtypes = [
+        _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, _P, c_int64, c_int, c_int, c_int, c_int,
+        c_int, POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_softmax_topk.argtypes = [
+        _P, c_int64, c_int, _P, _P, _P, c_int64, c_int, c_int, c_int, c_int, c_int, _P]
     lib.fnx_w4a16_nvfp4_gemv.argtypes = [
         _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
         c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),

@@ -598,6 +598,92 @@ int fnx_w8a16_gemv_norm_gated(const void* x, int64_t ldx, const void* z, int64_t
   return run_dense(c);
 }
 
+int fnx_router_gemv_topk(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                         const void* bias, float* logits, int64_t ldl, float* topk_weights,
+                         int32_t* topk_ids, int64_t ldk, int M, int N, int K, int topk,
+                         int renormalize, const fnx_workspace* ws, int pdl,
+                         fnx_stream_t stream) {
+  g_err.clear();
+  // router_gemv.py:60-80 (same conditions, same order of checks where they overlap)
+  if (M < 1 || M > FNX_MAX_M) return fail(FNX_EINVAL, "router GEMV requires 1 <= M <= 16");
+  if (K <= 0 || K % 128 || N <= 0 || N % 32)
+    return fail(FNX_EINVAL, "router GEMV requires matching K %% 128 == 0 and N %% 32 == 0");
+  if (!x || !w) return fail(FNX_EINVAL, "null x or weight");
+  if (!aligned(x, 16) || !aligned(w, 16) || ldx < K || ldw < K || ldx % 8 || ldw % 8)
+    return fail(FNX_EINVAL, "x and weight rows must be 16-byte aligned with ld >= K");
+  if (bias && !aligned(bias, 2)) return fail(FNX_EINVAL, "misaligned bias");
+  if (topk < 0 || topk > 32 || topk > N)
+    return fail(topk > 32 ? FNX_EUNSUPPORTED : FNX_EINVAL,
+                "topk=%d must be in [0, min(N, 32)]", topk);
+  if (topk > 0 && N > 512)
+    return fail(FNX_EUNSUPPORTED, "the fused top-k takes at most 512 experts (N=%d)", N);
+  if (topk > 0 && (!topk_weights || !topk_ids || ldk < topk))
+    return fail(FNX_EINVAL, "topk outputs must be [M, >= topk]");
+  if (topk > 0 && (!ws || !ws->counters || ws->n_counters < 1))
+    return fail(FNX_EINVAL, "the fused top-k needs a workspace counter");
+  float* lg = logits;
+  int64_t ld = ldl;
+  if (!lg) {
+    if (topk == 0) return fail(FNX_EINVAL, "null logits");
+    if (!ws->partials || ws->partial_floats < (int64_t)M * N)
+      return fail(FNX_EINVAL, "no logits buffer and the workspace holds fewer than M*N floats");
+    lg = ws->partials;
+    ld = N;
+  } else if (ldl < N) {
+    return fail(FNX_EINVAL, "ldl=%lld < N=%d", (long long)ldl, N);
+  }
+  fnx::RouterArgs a = {};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.w = static_cast<const __nv_bfloat16*>(w);
+  a.ldw = ldw;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.logits = lg;
+  a.ldl = ld;
+  a.out_w = topk_weights;
+  a.out_ids = topk_ids;
+  a.ldk = ldk;
+  a.counter = topk > 0 ? ws->counters : nullptr;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.topk = topk;
+  a.renorm = renormalize ? 1 : 0;
+  a.pdl = pdl;
+  if (fnx::launch_router(a, static_cast<cudaStream_t>(stream))) return cuda_fail("router launch");
+  return FNX_OK;
+}
+
+int fnx_softmax_topk(const void* scores, int64_t lds, int scores_f32, const float* bias,
+                     float* topk_weights, int32_t* topk_ids, int64_t ldk, int M, int N,
+                     int topk, int renormalize, int pdl, fnx_stream_t stream) {
+  g_err.clear();
+  if (M < 0 || N < 1 || N > 512)
+    return fail(N > 512 ? FNX_EUNSUPPORTED : FNX_EINVAL, "need M >= 0 and 1 <= N <= 512");
+  if (topk < 1 || topk > N || topk > 32)
+    return fail(topk > 32 && topk <= N ? FNX_EUNSUPPORTED : FNX_EINVAL,
+                "topk=%d must be in [1, min(N, 32)]", topk);
+  if (M == 0) return FNX_OK;
+  if (!scores || !topk_weights || !topk_ids || lds < N || ldk < topk)
+    return fail(FNX_EINVAL, "null or too narrow scores / outputs");
+  fnx::TopkArgs a = {};
+  a.scores = scores;
+  a.lds = lds;
+  a.scores_f32 = scores_f32 ? 1 : 0;
+  a.bias = bias;
+  a.out_w = topk_weights;
+  a.out_ids = topk_ids;
+  a.ldk = ldk;
+  a.M = M;
+  a.N = N;
+  a.topk = topk;
+  a.renorm = renormalize ? 1 : 0;
+  a.pdl = pdl;
+  if (fnx::launch_softmax_topk(a, static_cast<cudaStream_t>(stream)))
+    return cuda_fail("softmax top-k launch");
+  return FNX_OK;
+}
+
 int fnx_w4a16_nvfp4_gemv(const void* x, int64_t ldx, const void* wq, int64_t ldwq,
                          const void* bs, int64_t ldbs, const float* gscale,
                          int gscale_per_row, void* y, int64_t ldy, void* y2, int64_t ldy2,

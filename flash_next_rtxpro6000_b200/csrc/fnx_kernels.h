@@ -221,6 +221,38 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   return L;
 }
 
+// MoE router: x . W^T (+ bias) into fp32 logits, then (topk > 0) the softmax top-k of
+// every row, run by the CTA that finishes last (router.cu).
+struct RouterArgs {
+  const __nv_bfloat16* x;  // [M, K], row stride ldx elements, rows 16-byte aligned
+  int64_t ldx;
+  const __nv_bfloat16* w;  // [N, K] router weight, row stride ldw elements
+  int64_t ldw;
+  const __nv_bfloat16* bias;  // [N] or null
+  float* logits;           // [M, ldl] fp32
+  int64_t ldl;
+  float* out_w;            // [M, ldk] routing weights (topk > 0)
+  int32_t* out_ids;        // [M, ldk] expert ids
+  int64_t ldk;
+  unsigned* counter;       // CTA arrival counter, zero between calls (topk > 0)
+  int M, N, K, topk, renorm, pdl;
+};
+
+// Softmax top-k of given logits (bf16 or fp32 [M, lds]) plus an optional fp32 bias.
+struct TopkArgs {
+  const void* scores;
+  int64_t lds;
+  int scores_f32;
+  const float* bias;
+  float* out_w;
+  int32_t* out_ids;
+  int64_t ldk;
+  int M, N, topk, renorm, pdl;
+};
+
+int launch_router(const RouterArgs& a, cudaStream_t stream);
+int launch_softmax_topk(const TopkArgs& a, cudaStream_t stream);
+
 // Compiled forms of the dense kernel: whole activation rows staged; each CTA staging
 // only its k split (xslice); the fused gated RMSNorm (xslice or not, at run time).
 enum DenseMode : int { DENSE_PLAIN = 0, DENSE_SLICE = 1, DENSE_NORM = 2 };

@@ -18,6 +18,10 @@
  *   fnx_w8a16_gemv_silu_mul  w8a16_gemv.py:1009-1061 (w8a16_gemv_silu_mul)
  *   fnx_w8a16_gemv_norm_gated  w8a16_gemv.py:780-823 (w8a16_gemv_norm_gated; the norm
  *                            prologue of the kernel at :186-190, :220-233, :246-255)
+ *   fnx_router_gemv_topk     kernels/sglang/srt/layers/moe/router_gemv.py:10-93 (router_gemv,
+ *                            topk = 0) fused with the softmax top-k below (topk > 0)
+ *   fnx_softmax_topk         route_softmax_fast, patches/sglang/series/0110-moe-router-packed-
+ *                            key-softmax-top-k-SGLANG_ROUTER_FA.patch:27-184 as changed by 0111
  *   fnx_w4a16_nvfp4_gemv     kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:342-401
  *   fnx_moe_gemv             patches/sglang/series/0112-DG1-one-token-draft-MoE-as-a-W4A16-
  *                            NVFP4-Triton-GEMV.patch:328-386 (draft_moe_gemv), generalised
@@ -151,6 +155,32 @@ int fnx_w8a16_gemv_norm_gated(const void* x, int64_t ldx, const void* z, int64_t
                               int64_t ldy, int out_f32, int M, int N, int K,
                               const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
                               fnx_stream_t stream);
+
+/*
+ * MoE router.  logits[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]) in fp32 (bf16 inputs,
+ * no rounding of the result): x [M, K] and w [N, K] bf16 with 16-byte aligned rows
+ * (strides ldx, ldw in elements), bias bf16 [N] or NULL, 1 <= M <= 16, K % 128 == 0,
+ * N % 32 == 0.  With topk > 0 (<= 32, N <= 512) the same launch also writes the softmax
+ * top-k routing table (fnx_softmax_topk's rule) to topk_weights (fp32) and topk_ids
+ * (int32), both [M, ldk]; it then uses ws->counters[0] (zero between calls, left at zero)
+ * and, when logits is NULL, ws->partials as the logits buffer.
+ */
+int fnx_router_gemv_topk(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                         const void* bias, float* logits, int64_t ldl, float* topk_weights,
+                         int32_t* topk_ids, int64_t ldk, int M, int N, int K, int topk,
+                         int renormalize, const fnx_workspace* ws, int pdl,
+                         fnx_stream_t stream);
+
+/*
+ * Softmax top-k routing of given logits (bf16, or fp32 with scores_f32) plus an optional
+ * fp32 bias [N]: per row, weight[n] = exp(l[n] - max) / sum_n' exp(l[n'] - max); the topk
+ * largest l (NaN ranks as -1e30, -0.0 as +0.0; the lowest expert id wins ties) in
+ * descending order; with renormalize the picked weights are divided by their sum when it
+ * is positive.  N <= 512, topk <= min(N, 32).
+ */
+int fnx_softmax_topk(const void* scores, int64_t lds, int scores_f32, const float* bias,
+                     float* topk_weights, int32_t* topk_ids, int64_t ldk, int M, int N,
+                     int topk, int renormalize, int pdl, fnx_stream_t stream);
 
 /*
  * y[m, n] = bf16( (sum_k e2m1(wq[n, k]) * e4m3(bs[n, k / 16]) * x[m, k]) * gscale )

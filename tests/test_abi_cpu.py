@@ -127,3 +127,43 @@ def _norm_gated(**kw):
 def test_norm_gated_invalid_arguments_are_rejected(kw, code):
     assert _norm_gated(**kw) == code
     assert _lib.last_error()
+
+
+def _router(**kw):
+    args = dict(x=16, ldx=2048, w=16, ldw=2048, bias=None, logits=16, ldl=512, tw=16, ti=16,
+                ldk=10, M=1, N=512, K=2048, topk=10, renorm=1, ws=None, pdl=0, stream=None)
+    args.update(kw)
+    return _lib.lib().fnx_router_gemv_topk(*args.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(M=0), _lib.FNX_EINVAL),
+    (dict(M=17), _lib.FNX_EINVAL),
+    (dict(K=2000, ldx=2000, ldw=2000), _lib.FNX_EINVAL),   # K % 128
+    (dict(N=500), _lib.FNX_EINVAL),                         # N % 32
+    (dict(x=8), _lib.FNX_EINVAL),                           # misaligned rows
+    (dict(topk=33, N=1024, ldl=1024), _lib.FNX_EUNSUPPORTED),
+    (dict(topk=10, N=1024, ldl=1024), _lib.FNX_EUNSUPPORTED),  # > 512 experts for the top-k
+    (dict(topk=10, ws=None), _lib.FNX_EINVAL),              # the top-k needs the counter
+    (dict(topk=0, logits=None), _lib.FNX_EINVAL),
+    (dict(ldk=4), _lib.FNX_EINVAL),
+])
+def test_router_invalid_arguments_are_rejected(kw, code):
+    assert _router(**kw) == code
+    assert _lib.last_error()
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(N=513), _lib.FNX_EUNSUPPORTED),
+    (dict(topk=0), _lib.FNX_EINVAL),
+    (dict(topk=40, N=64), _lib.FNX_EUNSUPPORTED),
+    (dict(topk=65, N=64), _lib.FNX_EINVAL),
+    (dict(lds=10), _lib.FNX_EINVAL),
+])
+def test_softmax_topk_invalid_arguments_are_rejected(kw, code):
+    args = dict(s=16, lds=512, f32=0, bias=None, tw=16, ti=16, ldk=32, M=2, N=512, topk=10,
+                renorm=1, pdl=0, stream=None)
+    args.update(kw)
+    if "N" in kw and "lds" not in kw:
+        args["lds"] = max(args["N"], 1)
+    assert _lib.lib().fnx_softmax_topk(*args.values()) == code
