@@ -7,7 +7,7 @@ streams them from HBM.  Metric: HBM GB/s of algorithmic bytes (weights + scales 
 activations + logits + argmax), whole-job aggregate; µs per call is reported beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router]
+                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router|draft_step]
     python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
 
 With N > 1 (torchrun, one rank per GPU, NCCL) the lm_head is vocab-sharded: each rank
@@ -43,7 +43,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload",
-                    choices=["lm_head", "draft_head", "nvfp4", "moe", "norm_gated", "router"],
+                    choices=["lm_head", "draft_head", "nvfp4", "moe", "norm_gated", "router",
+                             "draft_step"],
                     default="lm_head")
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -230,6 +231,8 @@ def main():
         res = bench_norm_gated(args, fx, syn, dev)
     elif args.workload == "router":
         res = bench_router(args, fx, syn, dev)
+    elif args.workload == "draft_step":
+        res = bench_draft_step(args, fx, syn, dev)
     else:
         res = bench_moe(args, fx, syn, dev)
     if world > 1:
@@ -585,6 +588,61 @@ def bench_router(args, fx, syn, dev):
             "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"router_topk_{E}x{K}_top{k}", "M": Ms,
                        "l2": f"{copies} router-weight copies rotated in one CUDA graph (> 2x L2)"},
+            "per_m": per_m,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": None}
+
+
+def bench_draft_step(args, fx, syn, dev):
+    """The greedy draft step at the draft head's shape (49,152-token hot vocabulary, int8
+    49152 x 2048): draft_head_topk1 (GEMV + argmax + token map + draft_tokens + positions
+    in one launch) against w8a16_gemv followed by draft_topk1_postprocess (`unfused_us`).
+    3 weight copies (> 2x L2) rotated inside one CUDA graph."""
+    import torch
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    V, K, copies = syn.DRAFT_VOCAB, syn.HIDDEN, 3
+    head = syn.w8_head(V, K, seed=0)
+    ws = [head.w.to(dev)] + [head.w.to(dev) for _ in range(copies - 1)]
+    s = head.scale.to(dev)
+    hot = (torch.randperm(V, generator=torch.Generator().manual_seed(1)) + 1000).to(dev)
+    peak, src = measured_peak()
+    per_m, total_bytes, total_ms = {}, 0, 0.0
+    sampler = ClockSampler(_gpu_id(dev))
+    clocks = None
+    for M in Ms:
+        x = syn.activations(M, seed=1).to(dev)
+        pos = torch.zeros(M, dtype=torch.int64, device=dev)
+        dt = torch.zeros(M, 8, dtype=torch.int64, device=dev)
+        y = torch.empty(M, V, dtype=torch.bfloat16, device=dev)
+        n = 12  # calls per graph, rotating the copies
+        reps = max(3, args.steps // n)
+        res = {}
+        for name, fn in (("fused", lambda w: fx.draft_head_topk1(x, w, s, pos, dt, 1, hot,
+                                                                 out=y, pdl=True)),
+                         ("unfused", lambda w: fx.draft_topk1_postprocess(
+                             fx.w8a16_gemv(x, w, s, out=y, pdl=True), pos, dt, 1, hot,
+                             pdl=True))):
+            g = _graph_of([(lambda w=ws[i % copies]: fn(w)) for i in range(n)])
+            ms, ck = _timed(g.replay, reps, max(3, args.warmup // n), dev, 1,
+                            sampler if (M == Ms[-1] and name == "fused") else None)
+            clocks = ck or clocks
+            res[name] = (ms, ms / (reps * n) * 1e3)
+            del g
+        b = syn.w8_head_bytes(V, K, M) + 8 * V  # + the token map
+        us = res["fused"][1]
+        per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1),
+                         "unfused_us": round(res["unfused"][1], 3)}
+        total_bytes += b * reps * n
+        total_ms += res["fused"][0]
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8/bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"draft_step_{V}x{K}_hot_map", "M": Ms,
+                       "l2": f"{copies} weight copies rotated in one CUDA graph (> 2x L2)"},
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},

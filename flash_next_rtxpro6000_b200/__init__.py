@@ -11,6 +11,8 @@ the hand-written CUDA library ``_fnx.so``):
   down + router-weighted route sum), M <= 16;
 * ``router_gemv``, ``route_softmax_fast``, ``router_topk`` -- the MoE router projection
   and its softmax top-k routing table (fused into one launch by ``router_topk``);
+* ``draft_topk1_postprocess``, ``draft_head_topk1`` -- the greedy draft step with the
+  hot-vocabulary token map (the latter fused into the draft head's argmax);
 * ``sharded`` -- vocab-sharded lm_head and expert-sharded MoE over torch.distributed.
 """
 
@@ -44,5 +46,6 @@ from .draft_moe_gemv import (  # noqa: F401
 )
 
 from .router import covered, route_softmax_fast, router_gemv, router_topk  # noqa: F401
+from .draft_topk1 import draft_head_topk1, draft_topk1_postprocess  # noqa: F401
 
 __version__ = "0.1.0"

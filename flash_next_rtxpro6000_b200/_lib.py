@@ -27,6 +27,8 @@ EXPORTED = (
     "fnx_w8a16_gemv_norm_gated",
     "fnx_router_gemv_topk",
     "fnx_softmax_topk",
+    "fnx_draft_topk1",
+    "fnx_draft_head_topk1",
     "fnx_w4a16_nvfp4_gemv",
     "fnx_moe_workspace_bytes",
     "fnx_moe_gemv",
@@ -123,6 +125,13 @@ def _declare(lib):
         c_int, POINTER(FnxWorkspace), c_int, _P]
     lib.fnx_softmax_topk.argtypes = [
         _P, c_int64, c_int, _P, _P, _P, c_int64, c_int, c_int, c_int, c_int, c_int, _P]
+    lib.fnx_draft_topk1.argtypes = [
+        _P, c_int64, c_int, c_int, c_int, _P, _P, _P, c_int64, c_int, _P, _P,
+        POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_draft_head_topk1.argtypes = [
+        _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, c_int, c_int, c_int, c_int,
+        _P, _P, _P, c_int64, c_int, _P, _P, POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int,
+        _P]
     lib.fnx_w4a16_nvfp4_gemv.argtypes = [
         _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
         c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),

@@ -492,8 +492,11 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
         __threadfence();
         if (lane < M) {
           const unsigned long long key = atomicExch(&a.am_keys[lane], 0ull);
-          if (a.am_out) a.am_out[lane] = (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+          const int64_t row = (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+          if (a.am_out) a.am_out[lane] = row;
           if (a.am_key_out) a.am_key_out[lane] = key;
+          if (a.chain.topk_index || a.chain.topk_p || a.chain.draft_tokens || a.chain.positions)
+            draft_chain_store(a.chain, lane, row);
         }
         if (lane == 0) *a.am_count = 0u;
       }

@@ -250,6 +250,7 @@ struct DenseCall {
   int pdl;
   cudaStream_t stream;
   fnx::NormGate norm;  // gated RMSNorm on the activation load (norm.G > 0)
+  fnx::DraftChain chain;  // draft chain step on the argmax (all null: off)
 };
 
 int run_dense(const DenseCall& c) {
@@ -289,7 +290,9 @@ int run_dense(const DenseCall& c) {
   if (rc) return rc;
   const int NT = c.M > 8 ? 2 : 1;
 
-  const bool want_argmax = c.argmax_out || c.argmax_key_out;
+  const bool chain_on = c.chain.topk_index || c.chain.topk_p || c.chain.draft_tokens ||
+                        c.chain.positions;
+  const bool want_argmax = c.argmax_out || c.argmax_key_out || chain_on;
   if (p.ksplit > 1) {
     const int64_t need = (int64_t)p.tile_groups * p.ksplit * p.RT * 256;
     if (!c.ws || !c.ws->partials || !c.ws->counters)
@@ -372,6 +375,7 @@ int run_dense(const DenseCall& c) {
   a.n_units = p.n_units;
   a.pdl = c.pdl;
   a.norm = c.norm;
+  a.chain = c.chain;
   a.xslice = p.xslice;
   rc = fnx::launch_dense(a, c.wt, NT, p.CPW, grid, p.smem, c.stream);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no kernel instance for this configuration");
@@ -682,6 +686,82 @@ int fnx_softmax_topk(const void* scores, int64_t lds, int scores_f32, const floa
   if (fnx::launch_softmax_topk(a, static_cast<cudaStream_t>(stream)))
     return cuda_fail("softmax top-k launch");
   return FNX_OK;
+}
+
+namespace {
+
+// The draft chain arguments of fnx_draft_topk1 / fnx_draft_head_topk1.
+int make_chain(int M, const int64_t* hot_token_id, int64_t* positions, int64_t* draft_tokens,
+               int64_t ld_draft, int draft_col, int64_t* topk_index, float* topk_p,
+               fnx::DraftChain& c) {
+  if (draft_tokens && (draft_col < 0 || ld_draft <= draft_col))
+    return fail(FNX_EINVAL, "draft_token_column=%d outside a row of %lld", draft_col,
+                (long long)ld_draft);
+  if (!topk_index && !topk_p && !draft_tokens && !positions)
+    return fail(FNX_EINVAL, "no output of the draft step given");
+  c.token_map = hot_token_id;
+  c.topk_index = topk_index;
+  c.topk_p = topk_p;
+  c.draft_tokens = draft_tokens;
+  c.draft_ld = ld_draft;
+  c.draft_col = draft_col;
+  c.positions = positions;
+  (void)M;
+  return FNX_OK;
+}
+
+}  // namespace
+
+int fnx_draft_topk1(const void* logits, int64_t ldl, int logits_f32, int M, int V,
+                    const int64_t* hot_token_id, int64_t* positions, int64_t* draft_tokens,
+                    int64_t ld_draft, int draft_col, int64_t* topk_index, float* topk_p,
+                    const fnx_workspace* ws, int pdl, fnx_stream_t stream) {
+  g_err.clear();
+  if (M < 0 || M > FNX_MAX_M) return fail(FNX_EUNSUPPORTED, "M=%d must be in [0, 16]", M);
+  if (V < 1 || ldl < V) return fail(FNX_EINVAL, "bad logits shape V=%d ldl=%lld", V, (long long)ldl);
+  if (M == 0) return FNX_OK;
+  if (!logits) return fail(FNX_EINVAL, "null logits");
+  if (!ws || !ws->argmax_keys || !ws->argmax_count)
+    return fail(FNX_EINVAL, "the top-1 needs the workspace's argmax_keys/argmax_count");
+  fnx::Top1Args a = {};
+  if (int rc = make_chain(M, hot_token_id, positions, draft_tokens, ld_draft, draft_col,
+                          topk_index, topk_p, a.chain))
+    return rc;
+  a.logits = logits;
+  a.ldl = ldl;
+  a.logits_f32 = logits_f32 ? 1 : 0;
+  a.M = M;
+  a.V = V;
+  // slices of >= 4096 columns, about two CTAs per SM over all rows
+  const int want = std::max(1, (2 * fnx::num_sms()) / M);
+  a.splits = std::max(1, std::min(want, (V + 4095) / 4096));
+  a.pdl = pdl;
+  a.keys = ws->argmax_keys;
+  a.count = ws->argmax_count;
+  if (fnx::launch_top1(a, static_cast<cudaStream_t>(stream))) return cuda_fail("top-1 launch");
+  return FNX_OK;
+}
+
+int fnx_draft_head_topk1(const void* x, int64_t ldx, const void* w, int64_t ldw, int w_dtype,
+                         const void* scale, int scale_kind, void* logits, int64_t ldl,
+                         int out_f32, int M, int N, int K, const int64_t* hot_token_id,
+                         int64_t* positions, int64_t* draft_tokens, int64_t ld_draft,
+                         int draft_col, int64_t* topk_index, float* topk_p,
+                         const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                         fnx_stream_t stream) {
+  g_err.clear();
+  if (w_dtype != FNX_W_INT8 && w_dtype != FNX_W_FP8_E4M3 && w_dtype != FNX_W_BF16 &&
+      w_dtype != FNX_W_NVFP4)
+    return fail(FNX_EINVAL, "fnx_draft_head_topk1: bad w_dtype");
+  if (w_dtype == FNX_W_NVFP4)
+    return fail(FNX_EINVAL, "NVFP4 heads: use fnx_w4a16_nvfp4_gemv with argmax_out");
+  DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, logits, ldl, nullptr,
+                 0, 0, out_f32, nullptr, nullptr, 0, M, N, K, 0, cfg, ws, pdl,
+                 static_cast<cudaStream_t>(stream)};
+  if (int rc = make_chain(M, hot_token_id, positions, draft_tokens, ld_draft, draft_col,
+                          topk_index, topk_p, c.chain))
+    return rc;
+  return run_dense(c);
 }
 
 int fnx_w4a16_nvfp4_gemv(const void* x, int64_t ldx, const void* wq, int64_t ldwq,

@@ -10,6 +10,41 @@
 
 namespace fnx {
 
+// The greedy top-1 draft chain step applied to each token's argmax row (the finalize of
+// draft_topk1_postprocess, patches/sglang/series/0016-…patch:46-73): the row is mapped to
+// a full-vocabulary token through token_map (hot-vocabulary draft heads), written to
+// topk_index and to column draft_col of draft_tokens, topk_p is set to 1 and the
+// token's position advanced.  Every pointer may be null (that part is skipped).
+struct DraftChain {
+  const int64_t* token_map;  // [rows] int64, or null (token = row)
+  int64_t* topk_index;       // [M]
+  float* topk_p;             // [M]
+  int64_t* draft_tokens;     // [M, draft_ld]
+  int64_t draft_ld;
+  int draft_col;
+  int64_t* positions;        // [M], incremented
+};
+
+// Not inlined: it sits on the argmax path of every dense GEMV instance, where its code
+// would otherwise grow the kernels for a step only the draft head uses.  Arguments by
+// value (taking the address of a kernel's parameter block would copy it to the stack).
+static __device__ __noinline__ void draft_chain_store_v(const int64_t* token_map,
+                                                        int64_t* topk_index, float* topk_p,
+                                                        int64_t* draft_tokens, int64_t draft_ld,
+                                                        int draft_col, int64_t* positions, int m,
+                                                        int64_t row) {
+  const int64_t tok = token_map ? token_map[row] : row;
+  if (topk_index) topk_index[m] = tok;
+  if (topk_p) topk_p[m] = 1.f;
+  if (draft_tokens) draft_tokens[(size_t)m * draft_ld + draft_col] = tok;
+  if (positions) positions[m] += 1;
+}
+
+__device__ __forceinline__ void draft_chain_store(const DraftChain& c, int m, int64_t row) {
+  draft_chain_store_v(c.token_map, c.topk_index, c.topk_p, c.draft_tokens, c.draft_ld,
+                      c.draft_col, c.positions, m, row);
+}
+
 struct DenseArgs {
   const void* x;          // bf16 [M, K], row stride ldx elements, rows 16-byte aligned
   int64_t ldx;
@@ -50,6 +85,7 @@ struct DenseArgs {
   int pdl;
   int xslice;             // 1: gridDim.x % ksplit == 0, so each CTA stages (and sizes)
                           // only its k split of the activations
+  DraftChain chain;       // greedy draft-chain step on the argmax (all null: off)
   NormGate norm;          // gated RMSNorm on the activation load (norm.G > 0), else off;
                           // with xslice the unit k extent is a multiple of norm.G
 };
@@ -251,6 +287,21 @@ struct TopkArgs {
 };
 
 int launch_router(const RouterArgs& a, cudaStream_t stream);
+
+// Greedy top-1 of given logits rows (fp32 or bf16 [M, ldl], V columns) with the draft
+// chain step (topk1.cu): split over CTAs, keys combined with atomicMax, the last CTA
+// applies the chain and leaves keys and counter at zero.
+struct Top1Args {
+  const void* logits;
+  int64_t ldl;
+  int logits_f32;
+  int M, V, splits, pdl;
+  unsigned long long* keys;  // [M], zero between calls
+  unsigned* count;           // zero between calls
+  DraftChain chain;
+};
+
+int launch_top1(const Top1Args& a, cudaStream_t stream);
 int launch_softmax_topk(const TopkArgs& a, cudaStream_t stream);
 
 // Compiled forms of the dense kernel: whole activation rows staged; each CTA staging

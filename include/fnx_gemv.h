@@ -22,6 +22,10 @@
  *                            topk = 0) fused with the softmax top-k below (topk > 0)
  *   fnx_softmax_topk         route_softmax_fast, patches/sglang/series/0110-moe-router-packed-
  *                            key-softmax-top-k-SGLANG_ROUTER_FA.patch:27-184 as changed by 0111
+ *   fnx_draft_topk1          draft_topk1_postprocess (patches/sglang/series/0016-spec-remove-
+ *                            per-draft-step-glue-in-the-topk-1-chain-.patch:46-73: argmax,
+ *                            hot-vocabulary map, draft_tokens column, positions + 1)
+ *   fnx_draft_head_topk1     the draft head GEMV with the same step fused into its argmax
  *   fnx_w4a16_nvfp4_gemv     kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:342-401
  *   fnx_moe_gemv             patches/sglang/series/0112-DG1-one-token-draft-MoE-as-a-W4A16-
  *                            NVFP4-Triton-GEMV.patch:328-386 (draft_moe_gemv), generalised
@@ -181,6 +185,32 @@ int fnx_router_gemv_topk(const void* x, int64_t ldx, const void* w, int64_t ldw,
 int fnx_softmax_topk(const void* scores, int64_t lds, int scores_f32, const float* bias,
                      float* topk_weights, int32_t* topk_ids, int64_t ldk, int M, int N,
                      int topk, int renormalize, int pdl, fnx_stream_t stream);
+
+/*
+ * Greedy draft step on draft logits (fp32, or bf16 with logits_f32 == 0) [M, ldl], V
+ * columns, M <= 16: per row the argmax column (lowest on ties), mapped through
+ * hot_token_id (int64 [V], NULL: the column itself) to a token that is written to
+ * topk_index[m] and draft_tokens[m * ld_draft + draft_col]; topk_p[m] = 1 and
+ * positions[m] += 1.  Any of the four outputs may be NULL (not all).  Uses the workspace's
+ * argmax keys and counter (zero between calls, left at zero).
+ */
+int fnx_draft_topk1(const void* logits, int64_t ldl, int logits_f32, int M, int V,
+                    const int64_t* hot_token_id, int64_t* positions, int64_t* draft_tokens,
+                    int64_t ld_draft, int draft_col, int64_t* topk_index, float* topk_p,
+                    const fnx_workspace* ws, int pdl, fnx_stream_t stream);
+
+/*
+ * The draft head in one launch: logits = fnx_w8a16_gemv(x, w, scale) (bf16, or fp32
+ * holding bf16 values with out_f32) and fnx_draft_topk1's step on their bf16-rounded
+ * values, done by the GEMV's last CTA.  Arguments as those two entry points.
+ */
+int fnx_draft_head_topk1(const void* x, int64_t ldx, const void* w, int64_t ldw, int w_dtype,
+                         const void* scale, int scale_kind, void* logits, int64_t ldl,
+                         int out_f32, int M, int N, int K, const int64_t* hot_token_id,
+                         int64_t* positions, int64_t* draft_tokens, int64_t ld_draft,
+                         int draft_col, int64_t* topk_index, float* topk_p,
+                         const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                         fnx_stream_t stream);
 
 /*
  * y[m, n] = bf16( (sum_k e2m1(wq[n, k]) * e4m3(bs[n, k / 16]) * x[m, k]) * gscale )

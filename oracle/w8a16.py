@@ -112,3 +112,18 @@ def gemv_norm_gated(x_bf16, z_bf16, norm_weight, group_size, eps, w, kind, scale
     """bf16 logits of (gated_rmsnorm(x, z) @ w^T) * s (w8a16_gemv.py:780-823)."""
     xn = gated_rmsnorm(x_bf16, z_bf16, norm_weight, group_size, eps, sigmoid_gate)
     return gemv(xn, w, kind, scale)
+
+
+def draft_topk1(logits: np.ndarray, positions: np.ndarray, draft_tokens=None,
+                draft_token_column: int = 0, hot_token_id=None):
+    """draft_topk1_postprocess (patches/sglang/series/0016-…patch:46-73): the argmax of
+    each row (lowest column on ties), mapped through hot_token_id; returns (topk_p ones
+    [B, 1], topk_index [B, 1], new positions, new draft_tokens)."""
+    idx = argmax_lowest(np.asarray(logits, np.float64))
+    tok = idx if hot_token_id is None else np.asarray(hot_token_id)[idx]
+    dt = None
+    if draft_tokens is not None:
+        dt = np.array(draft_tokens, copy=True)
+        dt[:, draft_token_column] = tok
+    return (np.ones((len(idx), 1), np.float32), tok.reshape(-1, 1).astype(np.int64),
+            np.asarray(positions) + 1, dt)

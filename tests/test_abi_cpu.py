@@ -167,3 +167,22 @@ def test_softmax_topk_invalid_arguments_are_rejected(kw, code):
     if "N" in kw and "lds" not in kw:
         args["lds"] = max(args["N"], 1)
     assert _lib.lib().fnx_softmax_topk(*args.values()) == code
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(M=17), _lib.FNX_EUNSUPPORTED),
+    (dict(V=0), _lib.FNX_EINVAL),
+    (dict(ldl=10), _lib.FNX_EINVAL),
+    (dict(dt=16, ldd=3, col=3), _lib.FNX_EINVAL),   # column outside the row
+    (dict(ti=None, tp=None), _lib.FNX_EINVAL),      # nothing to write
+    (dict(ws=None), _lib.FNX_EINVAL),               # keys and counter live in the workspace
+])
+def test_draft_topk1_invalid_arguments_are_rejected(kw, code):
+    from flash_next_rtxpro6000_b200._lib import FnxWorkspace
+
+    fake = FnxWorkspace(16, 0, 16, 0, 16, 16, 16)  # checked for presence only, never read
+    args = dict(lg=16, ldl=1000, f32=1, M=2, V=1000, hot=None, pos=None, dt=None, ldd=0, col=0,
+                ti=16, tp=16, ws=ctypes.byref(fake), pdl=0, stream=None)
+    args.update(kw)
+    assert _lib.lib().fnx_draft_topk1(*args.values()) == code
+    assert _lib.last_error()
