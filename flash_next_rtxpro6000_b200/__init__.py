@@ -13,6 +13,8 @@ the hand-written CUDA library ``_fnx.so``):
   and its softmax top-k routing table (fused into one launch by ``router_topk``);
 * ``draft_topk1_postprocess``, ``draft_head_topk1`` -- the greedy draft step with the
   hot-vocabulary token map (the latter fused into the draft head's argmax);
+* ``nvfp4_dense`` -- the NVFP4 dense lm_head: load-time packing with an on-disk cache
+  and the linear method serving it through the NVFP4 GEMV;
 * ``sharded`` -- vocab-sharded lm_head and expert-sharded MoE over torch.distributed.
 """
 
