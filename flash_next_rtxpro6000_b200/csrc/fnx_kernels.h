@@ -217,7 +217,8 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   L.stage_bytes = dense_align(L.foff + 80, 128);
   int off = 0;
   L.bars = off;
-  off = dense_align(off + (3 * NS + 2 * RS) * 8, 128);  // full, converted, empty; rfull, rfree
+  // full, converted, empty; rfull, rfree; the activation rows' barrier
+  off = dense_align(off + (3 * NS + 2 * RS + 1) * 8, 128);
   L.stages = off;
   off += NS * L.stage_bytes;
   L.xs = off;

@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs 
   uint64_t* empty = full + 2 * NS;
   uint64_t* rfull = empty + NS;
   uint64_t* rfree = rfull + RS;
+  uint64_t* xbar = rfree + RS;  // bulk copy of the activation rows
   uint8_t* stages = smem + L.stages;
   uint8_t* xs = smem + L.xs;
   float* unscale = reinterpret_cast<float*>(smem + L.unscale);
@@ -226,10 +227,13 @@ __global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs 
       mbar_init(&rfull[r], W);
       mbar_init(&rfree[r], 1);
     }
+    mbar_init(xbar, 1);
     mbar_fence_init();
   }
   // x and topk_ids come from earlier kernels.
   pdl_wait();
+  // the activation rows travel by bulk copy while the routing table is decoded
+  if (tid == 0) issue_x_rows(xs, M, 0, H, reinterpret_cast<const __nv_bfloat16*>(a.x), a.ldx, xbar);
   route_decode(a, rt);  // ends with __syncthreads (also publishes the barrier inits)
   const int D = rt.misc[0];
   const int tiles = I / 8;
@@ -301,9 +305,9 @@ __global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs 
   }
   // The other warps stage the activations meanwhile; the producer never waits for them.
   if (warp > 0) {
-    stage_rows<W_NVFP4>(xs, unscale, M, 0, H, [&](int r) {
-      return reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)r * a.ldx;
-    }, 32, blockDim.x - 32, 1);
+    stage_rows_bulk<W_NVFP4, false>(xs, unscale, M, 0, H,
+                                    reinterpret_cast<const __nv_bfloat16*>(a.x), a.ldx,
+                                    NormGate{}, xbar, a.err, false, 32, blockDim.x - 32, 1);
     group_sync(1, blockDim.x - 32);
   }
 
