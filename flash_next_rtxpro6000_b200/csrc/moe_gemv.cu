@@ -235,6 +235,10 @@ __global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs 
   // the activation rows travel by bulk copy while the routing table is decoded
   if (tid == 0) issue_x_rows(xs, M, 0, H, reinterpret_cast<const __nv_bfloat16*>(a.x), a.ldx, xbar);
   route_decode(a, rt);  // ends with __syncthreads (also publishes the barrier inits)
+  // Every CTA is resident (the grid is one wave): the down kernel may launch now and take
+  // each SM as this grid's CTA there exits, decoding its routes and prefetching W2 while
+  // the other CTAs finish (it reads the act rows only after its griddepcontrol.wait).
+  pdl_trigger();
   const int D = rt.misc[0];
   const int tiles = I / 8;
   const int n_units = (D + a.has_shared) * tiles;
@@ -462,7 +466,6 @@ __global__ void __launch_bounds__(kMoeUpThreads, 1) moe_up_kernel(const MoeArgs 
         }
     }
   }
-  pdl_trigger();
 }
 
 // ------------------------------------------------------------------------------------
