@@ -177,6 +177,23 @@ int plan_dense(int M, int N, int K, int wt, int silu, const fnx_gemv_cfg* req, D
       }
     }
   }
+  // Large problems at M > 8 (two 8-token column blocks per tile): one row tile per unit
+  // and 8 consumer warps, which leaves shared memory for a deeper weight ring.  Measured
+  // on the int8 lm_head (151,936 x 2,048) at M = 16: 8 warps x 4 chunks x 1 tile 78.6 us,
+  // 16 x 4 x 2 (the cost model's pick) 92.6 us; at M <= 8 the cost model's pick is best.
+  if (NT == 2 && nch % 8 == 0 && nch / 8 <= 8 && ((nch / 8) & (nch / 8 - 1)) == 0) {
+    DensePlan q = p;
+    q.ksplit = 1;
+    q.nch_u = nch;
+    q.W = 8;
+    q.CPW = nch / 8;
+    q.RT = 1;
+    q.xslice = 0;
+    if (layout_plan(M, K, NT, q)) {
+      p = q;
+      return FNX_OK;
+    }
+  }
   // Search (k split, row tiles per unit RT, chunks per consumer warp CPW) with a cost
   // model of one CTA's time: rounds of units x the unit's chunk rows, plus a per-unit
   // overhead of each consumer warp (about 1.5 chunks) and of the split-K fix-up; fewer
