@@ -10,9 +10,10 @@ activations + logits + argmax), whole-job aggregate; µs per call is reported be
                     [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router|draft_step]
     python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
 
-With N > 1 (torchrun, one rank per GPU, NCCL) the lm_head is vocab-sharded: each rank
-streams V/N rows, computes its shard's argmax keys, and one NCCL MAX all-reduce of the
-keys gives the global greedy token (strong scaling: total work fixed).
+With N > 1 (torchrun, one rank per GPU) the lm_head is vocab-sharded: each rank streams
+V/N rows and computes its shard's greedy keys, and the MAX of the keys over ranks is taken
+inside the same launch over NVLink peer memory (``--exchange nccl``: an NCCL MAX
+all-reduce instead); strong scaling, total work fixed.
 """
 
 from __future__ import annotations
@@ -49,6 +50,9 @@ def parse_args():
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: greedy-key MAX inside the GEMV over NVLink (p2p) or by an "
+                         "NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -319,10 +323,24 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
     stream = torch.cuda.current_stream(dev).cuda_stream
     pdl = 1
 
+    from flash_next_rtxpro6000_b200 import sharded
+
+    p2p = world > 1 and args.exchange == "p2p"
+    ex = sharded.PeerExchange(dev) if p2p else None
+
     def call(i, x):
         # the operator API's C call, with the raw key output for the sharded reduction
         wc = wl[rot[0] % copies]
         rot[0] += 1
+        if p2p:  # the shard's GEMV with the greedy-key MAX over ranks in its last CTA
+            rc = lib.fnx_w8a16_gemv_vocab_sharded(
+                x.data_ptr(), x.stride(0), wc.data_ptr(), wc.stride(0), _lib.W_INT8,
+                s.data_ptr(), _lib.SCALE_BF16_ROW, ys[i].data_ptr(), ys[i].stride(0), 0,
+                ams[i].data_ptr(), r0, x.shape[0], shard, K, ex.buf, None, ctypes.byref(ws.c),
+                pdl, stream)
+            if rc:
+                raise RuntimeError(_lib.last_error())
+            return
         rc = lib.fnx_w8a16_gemv(
             x.data_ptr(), x.stride(0), wc.data_ptr(), wc.stride(0), _lib.W_INT8, s.data_ptr(),
             _lib.SCALE_BF16_ROW, ys[i].data_ptr(), ys[i].stride(0), None, 0, 0, 0,
@@ -335,7 +353,7 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
     def step():
         for i, x in enumerate(xs):
             call(i, x)
-            if world > 1:
+            if world > 1 and not p2p:
                 dist.all_reduce(keys[i], op=dist.ReduceOp.MAX)
                 lib.fnx_argmax_decode(keys[i].data_ptr(), ams[i].data_ptr(), x.shape[0], stream)
 
@@ -369,17 +387,22 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
                    "l2": f"{copies} weight cop{'y' if copies == 1 else 'ies'} of "
                          f"{shard * K / 1e6:.0f} MB rotated per call (>= 2x the 126 MB L2 "
                          "between reads of one copy), no flush",
-                   "parallelism": f"vocab-sharded x{world} + NCCL MAX all-reduce of argmax keys"
+                   "parallelism": (f"vocab-sharded x{world}, greedy-key MAX over NVLink peer "
+                                   "memory inside the GEMV" if p2p else
+                                   f"vocab-sharded x{world} + NCCL MAX all-reduce of argmax keys")
                    if world > 1 else "single GPU"},
         "us_per_call": {str(m): round(v, 3) for m, v in per_m.items()},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": tr, "peak_source": peak_src,
                      "kernel": "dense_gemv_kernel<int8>", "bytes_per_launch_avg": kbytes // len(Ms)},
         "clocks": clocks,
-        "gpu_launches": args.steps * len(Ms) * (2 if world > 1 else 1),
+        "gpu_launches": args.steps * len(Ms) * (2 if world > 1 and not p2p else 1),
     }
     if not args.no_e2e:
-        res["e2e"] = e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K)
+        res["e2e"] = e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K,
+                                 ex)
+    if ex is not None:
+        ex.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
 
@@ -399,7 +422,7 @@ def _lib_handle():
     return _lib.lib()
 
 
-def e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K):
+def e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K, ex=None):
     """Public API end to end: pinned host x -> device, w8a16_gemv(argmax_out=...),
     argmax -> pinned host, one host sync per step."""
     import torch
@@ -421,6 +444,8 @@ def e2e_lm_head(args, fx, syn, dev, wl, s, Ms, world, rank, r0, shard, V, K):
             dx[i].copy_(hx[i], non_blocking=True)
             if world == 1:
                 fx.w8a16_gemv(dx[i], w, s, out=ys[i], argmax_out=dam[i], pdl=True)
+            elif ex is not None:
+                sharded.vocab_sharded_lm_head(dx[i], w, s, r0, ex, out=ys[i], argmax_out=dam[i])
             else:
                 sharded.sharded_lm_head_argmax(dx[i], w, s, r0, out=ys[i], argmax_out=dam[i])
             ham[i].copy_(dam[i], non_blocking=True)

@@ -17,6 +17,7 @@ W_INT8, W_FP8_E4M3, W_BF16, W_NVFP4 = 0, 1, 2, 3
 SCALE_NONE, SCALE_F32_SCALAR, SCALE_F32_ROW, SCALE_BF16_SCALAR, SCALE_BF16_ROW = 0, 1, 2, 3, 4
 MAX_M = 16
 STATIC_PARTIAL_FLOATS, STATIC_COUNTERS = 256 * 1024, 2048  # fnx_w8a16_gemv_static_ws limits
+PEER_BUFFER_BYTES, IPC_HANDLE_BYTES, MAX_PEERS = 4096, 64, 8
 
 EXPORTED = (
     "fnx_plan_gemv",
@@ -29,6 +30,13 @@ EXPORTED = (
     "fnx_softmax_topk",
     "fnx_draft_topk1",
     "fnx_draft_head_topk1",
+    "fnx_peer_alloc",
+    "fnx_peer_free",
+    "fnx_ipc_get_handle",
+    "fnx_ipc_open",
+    "fnx_ipc_close",
+    "fnx_peer_setup",
+    "fnx_w8a16_gemv_vocab_sharded",
     "fnx_w4a16_nvfp4_gemv",
     "fnx_moe_workspace_bytes",
     "fnx_moe_gemv",
@@ -132,6 +140,15 @@ def _declare(lib):
         _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, c_int, c_int, c_int, c_int,
         _P, _P, _P, c_int64, c_int, _P, _P, POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int,
         _P]
+    lib.fnx_peer_alloc.argtypes = [POINTER(c_void_p)]
+    lib.fnx_peer_free.argtypes = [_P]
+    lib.fnx_ipc_get_handle.argtypes = [_P, _P]
+    lib.fnx_ipc_open.argtypes = [_P, POINTER(c_void_p)]
+    lib.fnx_ipc_close.argtypes = [_P]
+    lib.fnx_peer_setup.argtypes = [_P, POINTER(c_void_p), c_int, c_int]
+    lib.fnx_w8a16_gemv_vocab_sharded.argtypes = [
+        _P, c_int64, _P, c_int64, c_int, _P, c_int, _P, c_int64, c_int, _P, c_int64, c_int,
+        c_int, c_int, _P, POINTER(FnxGemvCfg), POINTER(FnxWorkspace), c_int, _P]
     lib.fnx_w4a16_nvfp4_gemv.argtypes = [
         _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
         c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),

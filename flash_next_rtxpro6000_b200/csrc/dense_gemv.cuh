@@ -490,8 +490,9 @@ __global__ void __launch_bounds__(kDenseThreadsMax, 1) dense_gemv_kernel(const D
       prev = __shfl_sync(0xffffffffu, prev, 0);
       if (prev == gridDim.x * (unsigned)E - 1) {
         __threadfence();
+        unsigned long long key = lane < M ? atomicExch(&a.am_keys[lane], 0ull) : 0ull;
+        if (a.peerbuf) key = peer_key_max(a.peerbuf, key, M, a.err);  // whole warp
         if (lane < M) {
-          const unsigned long long key = atomicExch(&a.am_keys[lane], 0ull);
           const int64_t row = (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
           if (a.am_out) a.am_out[lane] = row;
           if (a.am_key_out) a.am_key_out[lane] = key;

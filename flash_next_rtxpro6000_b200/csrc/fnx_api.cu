@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -268,6 +269,7 @@ struct DenseCall {
   cudaStream_t stream;
   fnx::NormGate norm;  // gated RMSNorm on the activation load (norm.G > 0)
   fnx::DraftChain chain;  // draft chain step on the argmax (all null: off)
+  unsigned char* peerbuf = nullptr;  // peer key exchange (vocab shards)
 };
 
 int run_dense(const DenseCall& c) {
@@ -309,7 +311,7 @@ int run_dense(const DenseCall& c) {
 
   const bool chain_on = c.chain.topk_index || c.chain.topk_p || c.chain.draft_tokens ||
                         c.chain.positions;
-  const bool want_argmax = c.argmax_out || c.argmax_key_out || chain_on;
+  const bool want_argmax = c.argmax_out || c.argmax_key_out || chain_on || c.peerbuf;
   if (p.ksplit > 1) {
     const int64_t need = (int64_t)p.tile_groups * p.ksplit * p.RT * 256;
     if (!c.ws || !c.ws->partials || !c.ws->counters)
@@ -393,6 +395,7 @@ int run_dense(const DenseCall& c) {
   a.pdl = c.pdl;
   a.norm = c.norm;
   a.chain = c.chain;
+  a.peerbuf = c.peerbuf;
   a.xslice = p.xslice;
   rc = fnx::launch_dense(a, c.wt, NT, p.CPW, grid, p.smem, c.stream);
   if (rc == 1) return fail(FNX_EUNSUPPORTED, "no kernel instance for this configuration");
@@ -778,6 +781,89 @@ int fnx_draft_head_topk1(const void* x, int64_t ldx, const void* w, int64_t ldw,
   if (int rc = make_chain(M, hot_token_id, positions, draft_tokens, ld_draft, draft_col,
                           topk_index, topk_p, c.chain))
     return rc;
+  return run_dense(c);
+}
+
+int fnx_peer_alloc(void** buf) {
+  g_err.clear();
+  if (!buf) return fail(FNX_EINVAL, "null output");
+  void* p = nullptr;
+  if (cudaMalloc(&p, FNX_PEER_BUFFER_BYTES) != cudaSuccess) return cuda_fail("cudaMalloc");
+  if (cudaMemset(p, 0, FNX_PEER_BUFFER_BYTES) != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail("cudaMemset");
+  }
+  *buf = p;
+  return FNX_OK;
+}
+
+int fnx_peer_free(void* buf) {
+  g_err.clear();
+  if (buf && cudaFree(buf) != cudaSuccess) return cuda_fail("cudaFree");
+  return FNX_OK;
+}
+
+int fnx_ipc_get_handle(void* buf, void* handle) {
+  g_err.clear();
+  if (!buf || !handle) return fail(FNX_EINVAL, "null argument");
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, buf) != cudaSuccess) return cuda_fail("cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == FNX_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return FNX_OK;
+}
+
+int fnx_ipc_open(const void* handle, void** buf) {
+  g_err.clear();
+  if (!handle || !buf) return fail(FNX_EINVAL, "null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return cuda_fail("cudaIpcOpenMemHandle");
+  *buf = p;
+  return FNX_OK;
+}
+
+int fnx_ipc_close(void* buf) {
+  g_err.clear();
+  if (buf && cudaIpcCloseMemHandle(buf) != cudaSuccess) return cuda_fail("cudaIpcCloseMemHandle");
+  return FNX_OK;
+}
+
+int fnx_peer_setup(void* local, void* const* bufs, int world, int rank) {
+  g_err.clear();
+  if (!local || !bufs || world < 1 || world > FNX_MAX_PEERS || rank < 0 || rank >= world)
+    return fail(FNX_EINVAL, "bad peer set (world=%d, rank=%d; at most %d ranks)", world, rank,
+                FNX_MAX_PEERS);
+  if (bufs[rank] != local) return fail(FNX_EINVAL, "bufs[rank] must be this rank's buffer");
+  fnx::PeerDesc d = {};
+  for (int r = 0; r < world; ++r) {
+    if (!bufs[r]) return fail(FNX_EINVAL, "null buffer of rank %d", r);
+    d.buf[r] = static_cast<unsigned char*>(bufs[r]);
+  }
+  d.world = world;
+  d.rank = rank;
+  if (cudaMemcpy(static_cast<unsigned char*>(local) + fnx::kPeerDescOff, &d, sizeof(d),
+                 cudaMemcpyHostToDevice) != cudaSuccess)
+    return cuda_fail("writing the peer table");
+  return FNX_OK;
+}
+
+int fnx_w8a16_gemv_vocab_sharded(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                 int w_dtype, const void* scale, int scale_kind, void* y,
+                                 int64_t ldy, int out_f32, int64_t* argmax_out,
+                                 int64_t row_offset, int M, int N, int K, void* peer_buf,
+                                 const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                                 fnx_stream_t stream) {
+  g_err.clear();
+  if (w_dtype != FNX_W_INT8 && w_dtype != FNX_W_FP8_E4M3 && w_dtype != FNX_W_BF16)
+    return fail(FNX_EINVAL, "fnx_w8a16_gemv_vocab_sharded: w_dtype must be int8, fp8_e4m3 or bf16");
+  if (!peer_buf) return fail(FNX_EINVAL, "null peer buffer");
+  DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, nullptr, 0,
+                 0, out_f32, argmax_out, nullptr, row_offset, M, N, K, 0, cfg, ws, pdl,
+                 static_cast<cudaStream_t>(stream)};
+  c.peerbuf = static_cast<unsigned char*>(peer_buf);
   return run_dense(c);
 }
 

@@ -45,6 +45,82 @@ __device__ __forceinline__ void draft_chain_store(const DraftChain& c, int m, in
                       c.draft_col, c.positions, m, row);
 }
 
+// Peer exchange of argmax keys for vocab-sharded heads (one process per GPU): every rank
+// holds one buffer (FNX_PEER_BUFFER_BYTES, zeroed at allocation) laid out as
+//   [0, 2048)     keys [2 (epoch parity)][8 ranks][16 tokens] u64, written by the ranks
+//   [2048, 2080)  flags [8 ranks] u32: the last epoch each rank has published here
+//   [2112, 2116)  epoch u32: this rank's call counter
+//   [2176, ...)   PeerDesc: every rank's buffer as mapped in this process, world, rank
+constexpr int kPeerFlagsOff = 2048, kPeerEpochOff = 2112, kPeerDescOff = 2176;
+struct PeerDesc {
+  unsigned char* buf[8];
+  int world, rank;
+};
+
+// The exchange step, done by one warp of the last CTA: lanes m < M hold this rank's key of
+// token m; returns the maximum over all ranks (the global greedy key).  Keys go to every
+// rank's buffer (slot of this call's epoch parity), then a release store of the epoch to
+// every rank's flag of this rank; the warp waits (acquire, bounded) until every rank has
+// published at least this epoch here and takes the maximum.  A rank can run at most one
+// call ahead of another (it needs the other's flag to finish a call), so two key slots
+// suffice.  An expired wait records ERR_WAIT_PEER and returns this rank's own key.
+static __device__ __noinline__ unsigned long long peer_key_max(unsigned char* pbuf,
+                                                               unsigned long long key, int M,
+                                                               int* err) {
+  const int lane = threadIdx.x & 31;
+  const PeerDesc* d = reinterpret_cast<const PeerDesc*>(pbuf + kPeerDescOff);
+  const int world = d->world, rank = d->rank;
+  unsigned* epoch_p = reinterpret_cast<unsigned*>(pbuf + kPeerEpochOff);
+  const unsigned e = *epoch_p + 1u;
+  const int par = e & 1u;
+  if (lane < M)
+    for (int r = 0; r < world; ++r) {
+      unsigned long long* dst =
+          reinterpret_cast<unsigned long long*>(d->buf[r]) + (par * 8 + rank) * 16 + lane;
+      asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(key) : "memory");
+    }
+  __syncwarp();
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  __syncwarp();
+  if (lane < world) {
+    unsigned* f = reinterpret_cast<unsigned*>(d->buf[lane] + kPeerFlagsOff) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+  }
+  bool ok = true;
+  if (lane < world) {
+    const unsigned* f = reinterpret_cast<const unsigned*>(pbuf + kPeerFlagsOff) + lane;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if ((int)(v - e) >= 0) break;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  if (!__all_sync(0xffffffffu, ok)) {
+    if (lane == 0) record_error(err, ERR_WAIT_PEER);
+  }
+  unsigned long long best = 0ull;
+  if (lane < M)
+    for (int r = 0; r < world; ++r) {
+      const unsigned long long* src =
+          reinterpret_cast<const unsigned long long*>(pbuf) + (par * 8 + r) * 16 + lane;
+      unsigned long long k;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(src) : "memory");
+      best = k > best ? k : best;
+    }
+  if (!ok) best = key;
+  __syncwarp();
+  if (lane == 0) *epoch_p = e;
+  return best;
+}
+
 struct DenseArgs {
   const void* x;          // bf16 [M, K], row stride ldx elements, rows 16-byte aligned
   int64_t ldx;
@@ -86,6 +162,7 @@ struct DenseArgs {
   int xslice;             // 1: gridDim.x % ksplit == 0, so each CTA stages (and sizes)
                           // only its k split of the activations
   DraftChain chain;       // greedy draft-chain step on the argmax (all null: off)
+  unsigned char* peerbuf; // this rank's peer-exchange buffer (vocab shards), or null
   NormGate norm;          // gated RMSNorm on the activation load (norm.G > 0), else off;
                           // with xslice the unit k extent is a multiple of norm.G
 };

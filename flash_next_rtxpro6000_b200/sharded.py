@@ -2,11 +2,13 @@
 
 One process per GPU.  Two sharding schemes, each with exactly one exchange step:
 
-* vocab-sharded lm_head (``sharded_lm_head_argmax``): rank g holds rows
-  [g*V/G, (g+1)*V/G).  The GEMV writes its shard's logits and a 64-bit argmax key per
-  token (bf16 value key << 32 | ~global_row); a MAX all-reduce of the M keys picks the
-  global greedy token with the lowest row on ties, bit-identical to the single-GPU
-  argmax because every rank rounds to bf16 before comparing.  ``all_gather_logits``
+* vocab-sharded lm_head: rank g holds rows [g*V/G, (g+1)*V/G).  The GEMV writes its
+  shard's logits and a 64-bit argmax key per token (bf16 value key << 32 | ~global_row);
+  the MAX of the M keys over ranks picks the global greedy token with the lowest row on
+  ties, bit-identical to the single-GPU argmax because every rank rounds to bf16 before
+  comparing.  ``vocab_sharded_lm_head`` does that MAX inside the GEMV's last CTA over
+  NVLink peer memory (``PeerExchange``, one launch per rank, no NCCL);
+  ``sharded_lm_head_argmax`` does it with an NCCL MAX all-reduce.  ``all_gather_logits``
   optionally assembles the full [M, V] logits.
 * expert-sharded MoE (``expert_sharded_moe``): rank g holds experts
   [g*E/G, (g+1)*E/G) (and rank 0 the shared expert).  Each rank computes the fp32 partial
@@ -70,6 +72,84 @@ def sharded_lm_head_argmax(x, w_shard, s_shard, row_offset: int, out=None, argma
     if dist.is_available() and dist.is_initialized():
         dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
     return y, decode_keys(keys, argmax_out)
+
+
+class PeerExchange:
+    """Buffers of the in-kernel greedy-key exchange (fnx_w8a16_gemv_vocab_sharded): one
+    small device buffer per rank, mapped into every other rank's process by CUDA IPC.
+    Collective over ``group`` (every rank constructs it together); ``close`` likewise.
+    Without an initialised process group it is the one-rank exchange (with itself)."""
+
+    def __init__(self, device=None, group=None):
+        self.group = group
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        multi = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if multi else 1
+        self.rank = dist.get_rank(group) if multi else 0
+        if self.world > _lib.MAX_PEERS:
+            raise NotImplementedError(f"at most {_lib.MAX_PEERS} ranks")
+        lib = _lib.lib()
+        with torch.cuda.device(self.device):
+            buf = ctypes.c_void_p()
+            check(lib.fnx_peer_alloc(ctypes.byref(buf)), "fnx_peer_alloc")
+            self.buf = buf.value
+            handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+            check(lib.fnx_ipc_get_handle(self.buf, handle), "fnx_ipc_get_handle")
+            handles = [None] * self.world
+            if multi:
+                dist.all_gather_object(handles, handle.raw, group=group)
+            else:
+                handles[0] = handle.raw
+            self.opened = []
+            bufs = (ctypes.c_void_p * self.world)()
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bufs[r] = self.buf
+                    continue
+                p = ctypes.c_void_p()
+                check(lib.fnx_ipc_open(ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES),
+                                       ctypes.byref(p)), "fnx_ipc_open")
+                bufs[r] = p.value
+                self.opened.append(p.value)
+            check(lib.fnx_peer_setup(self.buf, bufs, self.world, self.rank), "fnx_peer_setup")
+        if multi:
+            dist.barrier(group=group)
+
+    def close(self):
+        """Unmap the other ranks' buffers and free this rank's (after every rank's last
+        call has finished)."""
+        if self.buf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if dist.is_available() and dist.is_initialized():
+            dist.barrier(group=self.group)
+        lib = _lib.lib()
+        with torch.cuda.device(self.device):
+            for p in self.opened:
+                check(lib.fnx_ipc_close(p), "fnx_ipc_close")
+            check(lib.fnx_peer_free(self.buf), "fnx_peer_free")
+        self.opened, self.buf = [], None
+
+
+def vocab_sharded_lm_head(x, w_shard, s_shard, row_offset: int, exchange: PeerExchange,
+                          out=None, argmax_out=None, pdl: Optional[bool] = True):
+    """Greedy token of a vocab-sharded head in one launch per rank: the shard's GEMV with
+    the MAX over ranks of the greedy keys done by its last CTA over NVLink (no NCCL)."""
+    M, K = x.shape
+    N = w_shard.shape[0]
+    x = _activation(x)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device) if out is None else out
+    am = torch.empty(M, dtype=torch.int64, device=x.device) if argmax_out is None else argmax_out
+    s, skind = _scale_kind(s_shard, N)
+    ws = _workspace(x.device)
+    rc = _lib.lib().fnx_w8a16_gemv_vocab_sharded(
+        ptr(x), x.stride(0), ptr(w_shard), w_shard.stride(0) * w_shard.element_size(),
+        _weight_kind(w_shard), ptr(s), skind, ptr(y), y.stride(0), int(y.dtype == torch.float32),
+        ptr(am), row_offset, M, N, K, exchange.buf, None, ctypes.byref(ws.c),
+        int(PDL if pdl is None else pdl), _stream(x))
+    check(rc, "vocab_sharded_lm_head")
+    return y, am
 
 
 def all_gather_logits(local: torch.Tensor, group=None) -> torch.Tensor:

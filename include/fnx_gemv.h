@@ -26,6 +26,10 @@
  *                            per-draft-step-glue-in-the-topk-1-chain-.patch:46-73: argmax,
  *                            hot-vocabulary map, draft_tokens column, positions + 1)
  *   fnx_draft_head_topk1     the draft head GEMV with the same step fused into its argmax
+ *   fnx_w8a16_gemv_vocab_sharded  the vocab-sharded lm_head with the greedy token's MAX
+ *                            reduction over ranks fused into the GEMV (the NCCL all-reduce
+ *                            of argmax keys it replaces has no counterpart in the reference,
+ *                            which serves one GPU); fnx_peer_* / fnx_ipc_* set its buffers up
  *   fnx_w4a16_nvfp4_gemv     kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:342-401
  *   fnx_moe_gemv             patches/sglang/series/0112-DG1-one-token-draft-MoE-as-a-W4A16-
  *                            NVFP4-Triton-GEMV.patch:328-386 (draft_moe_gemv), generalised
@@ -211,6 +215,35 @@ int fnx_draft_head_topk1(const void* x, int64_t ldx, const void* w, int64_t ldw,
                          int draft_col, int64_t* topk_index, float* topk_p,
                          const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
                          fnx_stream_t stream);
+
+/*
+ * Vocab-sharded lm_head, one process per GPU on one node.  Each rank allocates one
+ * FNX_PEER_BUFFER_BYTES device buffer (fnx_peer_alloc, zeroed), exports it
+ * (fnx_ipc_get_handle, FNX_IPC_HANDLE_BYTES), opens the other ranks' handles
+ * (fnx_ipc_open) and records all of them (fnx_peer_setup, bufs[r] = rank r's buffer as
+ * mapped in this process, bufs[rank] = its own).  fnx_w8a16_gemv_vocab_sharded then
+ * computes its shard's logits like fnx_w8a16_gemv (rows row_offset + n) and, in the same
+ * launch, exchanges the greedy keys with every rank over NVLink and writes the global
+ * greedy row to argmax_out on every rank.  All ranks must make the same sequence of calls;
+ * a rank that waits more than 2 s for the others records an error code in ws->error_flag
+ * and returns its own shard's token.  Calls on one rank are ordered on one stream.
+ * At most FNX_MAX_PEERS ranks, M <= 16.
+ */
+#define FNX_PEER_BUFFER_BYTES 4096
+#define FNX_IPC_HANDLE_BYTES 64
+#define FNX_MAX_PEERS 8
+int fnx_peer_alloc(void** buf);
+int fnx_peer_free(void* buf);
+int fnx_ipc_get_handle(void* buf, void* handle);
+int fnx_ipc_open(const void* handle, void** buf);
+int fnx_ipc_close(void* buf);
+int fnx_peer_setup(void* local, void* const* bufs, int world, int rank);
+int fnx_w8a16_gemv_vocab_sharded(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                 int w_dtype, const void* scale, int scale_kind, void* y,
+                                 int64_t ldy, int out_f32, int64_t* argmax_out,
+                                 int64_t row_offset, int M, int N, int K, void* peer_buf,
+                                 const fnx_gemv_cfg* cfg, const fnx_workspace* ws, int pdl,
+                                 fnx_stream_t stream);
 
 /*
  * y[m, n] = bf16( (sum_k e2m1(wq[n, k]) * e4m3(bs[n, k / 16]) * x[m, k]) * gscale )

@@ -1,5 +1,6 @@
-"""Sharded forms on 2 GPUs (NCCL), against the 1-GPU results: the vocab-sharded lm_head
-(MAX all-reduce of argmax keys) gives the same greedy tokens and the same logits, and
+"""Sharded forms on 2 GPUs, against the 1-GPU results: the vocab-sharded lm_head (NCCL
+MAX all-reduce of argmax keys, and the exchange inside the GEMV over NVLink peer memory
+on three calls in a row) gives the same greedy tokens and the same logits, and
 the expert-sharded MoE (SUM all-reduce of fp32 expert-slice partials) matches the
 whole layer.  Skipped on a box with fewer than 2 GPUs.
 
@@ -37,9 +38,21 @@ def _rank_main(rank, world, port, q):
         head = syn.w8_head(V, K, seed=3)
         x = syn.activations(M, seed=4).to(dev)
         r0, n = sharded.shard_rows(V, world, rank)
-        y, am = sharded.sharded_lm_head_argmax(x, head.w[r0:r0 + n].contiguous().to(dev),
-                                               head.scale[r0:r0 + n].contiguous().to(dev), r0)
+        w_sh = head.w[r0:r0 + n].contiguous().to(dev)
+        s_sh = head.scale[r0:r0 + n].contiguous().to(dev)
+        y, am = sharded.sharded_lm_head_argmax(x, w_sh, s_sh, r0)
         full = sharded.all_gather_logits(y)
+        # the same greedy tokens with the exchange inside the GEMV (NVLink peer memory),
+        # three calls in a row (epochs 1..3, both key slots)
+        ex = sharded.PeerExchange(dev)
+        am_p2p = []
+        for rep in range(3):
+            xr = syn.activations(M, seed=4 + rep).to(dev)
+            _, a2 = sharded.vocab_sharded_lm_head(xr, w_sh, s_sh, r0, ex)
+            am_p2p.append(a2.cpu())
+        from flash_next_rtxpro6000_b200.w8a16_gemv import _workspace
+        p2p_err = int(_workspace(dev).error_flag.item())
+        ex.close()
         # expert-sharded MoE
         E = 64
         L = syn.moe_layer(E, 2048, 512, seed=5)
@@ -63,11 +76,11 @@ def _rank_main(rank, world, port, q):
             workspace=ws, shared_expert=shared)
         torch.cuda.synchronize()
         if rank == 0:
-            q.put(("ok", am.cpu(), full.cpu(), moe.cpu()))
+            q.put(("ok", am.cpu(), full.cpu(), moe.cpu(), am_p2p, p2p_err))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:  # report to the parent instead of hanging it
-        q.put(("error", traceback.format_exc(), None, None))
+        q.put(("error", traceback.format_exc(), None, None, None, None))
 
 
 def _single_gpu_reference():
@@ -81,6 +94,12 @@ def _single_gpu_reference():
     x = syn.activations(M, seed=4).to(dev)
     am = torch.empty(M, dtype=torch.int64, device=dev)
     y = fx.w8a16_gemv(x, head.w.to(dev), head.scale.to(dev), argmax_out=am)
+    am_reps = []
+    for rep in range(3):
+        a = torch.empty(M, dtype=torch.int64, device=dev)
+        fx.w8a16_gemv(syn.activations(M, seed=4 + rep).to(dev), head.w.to(dev),
+                      head.scale.to(dev), argmax_out=a)
+        am_reps.append(a.cpu())
     E = 64
     L = syn.moe_layer(E, 2048, 512, seed=5)
     ids, wts = syn.routing(M, E=E, seed=6)
@@ -95,7 +114,7 @@ def _single_gpu_reference():
         w2_blockscale_swizzled=swizzle_blockscale(L.s2.to(dev)), w2_weight_scale_2=L.g2.to(dev),
         workspace=ws, shared_expert=shared, out_f32=True)
     torch.cuda.synchronize()
-    return am.cpu(), y.cpu(), moe.cpu()
+    return am.cpu(), y.cpu(), moe.cpu(), am_reps
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2 if torch.cuda.is_available() else True,
@@ -103,7 +122,7 @@ def _single_gpu_reference():
 def test_two_rank_sharded_head_and_moe():
     import torch.multiprocessing as mp
 
-    am1, y1, moe1 = _single_gpu_reference()
+    am1, y1, moe1, am_reps = _single_gpu_reference()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29600 + os.getpid() % 200
@@ -111,7 +130,7 @@ def test_two_rank_sharded_head_and_moe():
     for p in procs:
         p.start()
     try:
-        status, am, full, moe = q.get(timeout=240)
+        status, am, full, moe, am_p2p, p2p_err = q.get(timeout=240)
     finally:
         for p in procs:
             p.join(timeout=60)
@@ -119,6 +138,9 @@ def test_two_rank_sharded_head_and_moe():
                 p.kill()
     assert status == "ok", am
     assert torch.equal(am, am1)
+    assert p2p_err == 0
+    for got, ref in zip(am_p2p, am_reps):
+        assert torch.equal(got, ref)
     # a shard may be tiled differently (its own plan), which can move an fp32 sum by an
     # ulp before the bf16 rounding
     assert float((full.float() - y1.float()).abs().max() / y1.float().abs().max()) <= 2e-2
