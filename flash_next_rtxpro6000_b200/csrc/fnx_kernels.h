@@ -48,22 +48,25 @@ __device__ __forceinline__ void draft_chain_store(const DraftChain& c, int m, in
 // Peer exchange of argmax keys for vocab-sharded heads (one process per GPU): every rank
 // holds one buffer (FNX_PEER_BUFFER_BYTES, zeroed at allocation) laid out as
 //   [0, 2048)     keys [2 (epoch parity)][8 ranks][16 tokens] u64, written by the ranks
-//   [2048, 2080)  flags [8 ranks] u32: the last epoch each rank has published here
-//   [2112, 2116)  epoch u32: this rank's call counter
-//   [2176, ...)   PeerDesc: every rank's buffer as mapped in this process, world, rank
-constexpr int kPeerFlagsOff = 2048, kPeerEpochOff = 2112, kPeerDescOff = 2176;
+//   [2048, 2560)  flags [8 ranks][16 tokens] u32: the last epoch rank r published token m
+//   [2560, 2564)  epoch u32: this rank's call counter
+//   [2624, ...)   PeerDesc: every rank's buffer as mapped in this process, world, rank
+constexpr int kPeerFlagsOff = 2048, kPeerEpochOff = 2560, kPeerDescOff = 2624;
 struct PeerDesc {
   unsigned char* buf[8];
   int world, rank;
 };
 
-// The exchange step, done by one warp of the last CTA: lanes m < M hold this rank's key of
-// token m; returns the maximum over all ranks (the global greedy key).  Keys go to every
-// rank's buffer (slot of this call's epoch parity), then a release store of the epoch to
-// every rank's flag of this rank; the warp waits (acquire, bounded) until every rank has
-// published at least this epoch here and takes the maximum.  A rank can run at most one
-// call ahead of another (it needs the other's flag to finish a call), so two key slots
-// suffice.  An expired wait records ERR_WAIT_PEER and returns this rank's own key.
+// The exchange step, done by one warp of the last CTA: lane m < M holds this rank's key of
+// token m and returns the maximum over all ranks (the global greedy key).  Lane m writes
+// its key into every rank's buffer (slot of this call's epoch parity), fences at system
+// scope once and writes the epoch into every rank's flag of (this rank, token m) (a
+// release pattern: the fence orders its key stores before the flags); it then polls its
+// own buffer's flags of token m with acquire loads until every rank has published at
+// least this epoch, and reads the keys.  No cross-lane ordering is needed: each lane pairs
+// its own stores and loads.  A rank can run at most one call ahead of another (it needs the
+// other's flags to finish a call), so two key slots suffice.  An expired wait (2 s)
+// records ERR_WAIT_PEER and returns this rank's own key.
 static __device__ __noinline__ unsigned long long peer_key_max(unsigned char* pbuf,
                                                                unsigned long long key, int M,
                                                                int* err) {
@@ -73,50 +76,46 @@ static __device__ __noinline__ unsigned long long peer_key_max(unsigned char* pb
   unsigned* epoch_p = reinterpret_cast<unsigned*>(pbuf + kPeerEpochOff);
   const unsigned e = *epoch_p + 1u;
   const int par = e & 1u;
-  if (lane < M)
+  unsigned long long best = key;
+  bool ok = true;
+  if (lane < M) {
     for (int r = 0; r < world; ++r) {
       unsigned long long* dst =
           reinterpret_cast<unsigned long long*>(d->buf[r]) + (par * 8 + rank) * 16 + lane;
       asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(key) : "memory");
     }
-  __syncwarp();
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  __syncwarp();
-  if (lane < world) {
-    unsigned* f = reinterpret_cast<unsigned*>(d->buf[lane] + kPeerFlagsOff) + rank;
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-  }
-  bool ok = true;
-  if (lane < world) {
-    const unsigned* f = reinterpret_cast<const unsigned*>(pbuf + kPeerFlagsOff) + lane;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if ((int)(v - e) >= 0) break;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        ok = false;
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  __syncwarp();
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  if (!__all_sync(0xffffffffu, ok)) {
-    if (lane == 0) record_error(err, ERR_WAIT_PEER);
-  }
-  unsigned long long best = 0ull;
-  if (lane < M)
+    // one system-scope fence, then plain (relaxed) flag stores: a release pattern that
+    // orders this lane's key stores before every flag at the cost of a single fence
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int r = 0; r < world; ++r) {
-      const unsigned long long* src =
-          reinterpret_cast<const unsigned long long*>(pbuf) + (par * 8 + r) * 16 + lane;
-      unsigned long long k;
-      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(src) : "memory");
-      best = k > best ? k : best;
+      unsigned* f = reinterpret_cast<unsigned*>(d->buf[r] + kPeerFlagsOff) + rank * 16 + lane;
+      asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
     }
-  if (!ok) best = key;
-  __syncwarp();
+    const unsigned long long t0 = global_ns();
+    for (int r = 0; r < world && ok; ++r) {
+      if (r == rank) continue;
+      const unsigned* f = reinterpret_cast<const unsigned*>(pbuf + kPeerFlagsOff) + r * 16 + lane;
+      for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if ((int)(v - e) >= 0) break;
+        if (global_ns() - t0 > kWaitLimitNs) {
+          ok = false;
+          break;
+        }
+        __nanosleep(32);
+      }
+      if (ok) {
+        unsigned long long k;
+        const unsigned long long* src =
+            reinterpret_cast<const unsigned long long*>(pbuf) + (par * 8 + r) * 16 + lane;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(src) : "memory");
+        best = k > best ? k : best;
+      }
+    }
+    if (!ok) best = key;
+  }
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) record_error(err, ERR_WAIT_PEER);
   if (lane == 0) *epoch_p = e;
   return best;
 }
