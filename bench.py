@@ -7,7 +7,8 @@ streams them from HBM.  Metric: HBM GB/s of algorithmic bytes (weights + scales 
 activations + logits + argmax), whole-job aggregate; µs per call is reported beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router|draft_step]
+                    [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router|draft_step|stack]
+                    [--layers L]   # stack: L MoE layers + the lm_head per step (default 48)
     python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
 
 With N > 1 (torchrun, one rank per GPU) the lm_head is vocab-sharded: each rank streams
@@ -45,9 +46,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload",
                     choices=["lm_head", "draft_head", "nvfp4", "moe", "norm_gated", "router",
-                             "draft_step"],
+                             "draft_step", "stack"],
                     default="lm_head")
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
+    ap.add_argument("--layers", type=int, default=48, help="MoE layers of --workload stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
@@ -237,8 +239,11 @@ def main():
         res = bench_router(args, fx, syn, dev)
     elif args.workload == "draft_step":
         res = bench_draft_step(args, fx, syn, dev)
+    elif args.workload == "stack":
+        res = bench_stack(args, fx, syn, dev)
     else:
-        res = bench_moe(args, fx, syn, dev)
+        res = (bench_moe_sharded(args, fx, syn, dev, rank, world) if world > 1
+               else bench_moe(args, fx, syn, dev))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -696,6 +701,7 @@ def bench_moe(args, fx, syn, dev):
     sampler = ClockSampler(_gpu_id(dev))
     clocks = None
     n_rot = 48
+    launches = 0
     for M in Ms:
         rots, nbytes = [], 0
         for r in range(n_rot):
@@ -727,6 +733,7 @@ def bench_moe(args, fx, syn, dev):
                            "bytes_per_call": int(bytes_per_call)}
         total_bytes += bytes_per_call * reps * n_rot
         total_ms += ms
+        launches += reps * n_rot * 3  # k1, k2, route sum
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
@@ -738,7 +745,192 @@ def bench_moe(args, fx, syn, dev):
             "per_m": results,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": None}
+            "clocks": clocks, "gpu_launches": launches}
+
+
+def _device_moe_layer(fx, syn, dev, seed, experts=None):
+    """One config-2 MoE layer (512 experts + shared expert) generated on the device: code
+    bytes uniform over 0-255, e4m3 block scales |N(0,1)|*0.5, global scales 1/448.  The
+    scales are drawn directly in the 128x4-swizzled order (a fixed permutation of
+    independent draws has the same distribution), so no swizzle pass is needed."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    E, H, I = experts or syn.EXPERTS, syn.HIDDEN, syn.INTER
+
+    def codes(*shape):
+        return torch.randint(0, 256, shape, generator=g, dtype=torch.uint8, device=dev)
+
+    def scales(*shape):
+        s = torch.randn(*shape, generator=g, device=dev).abs_().mul_(0.5)
+        return s.to(torch.float8_e4m3fn).view(torch.uint8)
+
+    gs = 1.0 / 448.0
+    d = dict(w13=codes(E, 2 * I, H // 2), s13=scales(E, 2 * I, H // 16),
+             g13=torch.full((E, 2), gs, device=dev), w2=codes(E, H, I // 2),
+             s2=scales(E, H, I // 16), g2=torch.full((E,), gs, device=dev))
+    shared = fx.SharedExpert(codes(1, 2 * I, H // 2), scales(1, 2 * I, H // 16),
+                             torch.tensor([gs], device=dev), codes(1, H, I // 2),
+                             scales(1, H, I // 16), torch.tensor([gs], device=dev))
+    return d, shared
+
+
+def bench_stack(args, fx, syn, dev):
+    """Config 3: a decode step of 48 MoE layers (config 2 each, with its own weights:
+    about 43.5 GB of NVFP4 resident) chained layer to layer, ending in the config-1 int8
+    lm_head with greedy argmax.  One CUDA graph per M holds the whole step; the step's
+    weights are far larger than L2, so every layer streams from HBM."""
+    import torch
+
+    Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
+    n_layers = args.layers
+    layers = [_device_moe_layer(fx, syn, dev, seed=layer) for layer in range(n_layers)]
+    head = syn.w8_head(syn.VOCAB, syn.HIDDEN, seed=0)
+    hw, hs = head.w.to(dev), head.scale.to(dev)
+    del head
+    ws = fx.make_workspace(num_routes=syn.TOPK, hidden_size=syn.HIDDEN,
+                           intermediate_size=syn.INTER, device=dev)
+    moe_cfg = fx.DraftMoeGemvConfig(pdl=True)
+    peak, src = measured_peak()
+    sampler = ClockSampler(_gpu_id(dev))
+    clocks = None
+    per_m, total_bytes, total_ms, launches = {}, 0, 0.0, 0
+    reps = max(5, min(args.steps, 50))
+    for M in Ms:
+        routes, step_bytes = [], syn.w8_head_bytes(syn.VOCAB, syn.HIDDEN, M)
+        for layer in range(n_layers):
+            ids, wts = syn.routing(M, E=syn.EXPERTS, seed=100_000 + 1000 * M + layer)
+            step_bytes += syn.moe_bytes(int(torch.unique(ids).numel()), M=M)
+            routes.append((ids.to(dev), wts.to(dev)))
+        bufs = [syn.activations(M, seed=3).to(dev),
+                torch.empty(M, syn.HIDDEN, dtype=torch.bfloat16, device=dev)]
+        logits = torch.empty(M, syn.VOCAB, dtype=torch.bfloat16, device=dev)
+        am = torch.empty(M, dtype=torch.int64, device=dev)
+
+        def layer_call(layer):
+            (d, shared), (ids, wts) = layers[layer], routes[layer]
+            fx.draft_moe_gemv(hidden_states=bufs[layer % 2], topk_ids=ids, topk_weights=wts,
+                              w13_weight=d["w13"], w13_blockscale_swizzled=d["s13"],
+                              w13_weight_scale_2=d["g13"], w2_weight=d["w2"],
+                              w2_blockscale_swizzled=d["s2"], w2_weight_scale_2=d["g2"],
+                              workspace=ws, shared_expert=shared, out=bufs[(layer + 1) % 2],
+                              cfg=moe_cfg)
+
+        calls = [(lambda layer=layer: layer_call(layer)) for layer in range(n_layers)]
+        calls.append(lambda: fx.w8a16_gemv(bufs[n_layers % 2], hw, hs, out=logits,
+                                           argmax_out=am, pdl=True))
+        g = _graph_of(calls)
+        ms, ck = _timed(g.replay, reps, max(3, args.warmup // 10), dev, 1,
+                        sampler if M == Ms[-1] else None)
+        clocks = ck or clocks
+        us = ms / reps * 1e3
+        per_m[str(M)] = {"us_per_step": round(us, 2),
+                         "GBps": round(step_bytes / (us * 1e-6) / 1e9, 1),
+                         "bytes_per_step": int(step_bytes),
+                         "argmax": am.cpu().tolist()}
+        total_bytes += step_bytes * reps
+        total_ms += ms
+        launches += reps * (3 * n_layers + 1)  # k1, k2, route sum per layer; lm_head
+        del g
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+            "steps": reps * len(Ms), "warmup": args.warmup,
+            "ms_per_step": round(total_ms / (reps * len(Ms)), 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4+int8/bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"decode_stack_{n_layers}x_moe512x2048x512_top10_shared"
+                                   f"+lm_head{syn.VOCAB}", "M": Ms, "layers": n_layers,
+                       "l2": "whole step's weights (about 0.91 GB per layer) far above L2",
+                       "chain": "layer l output is layer l+1 input; the last feeds the lm_head"},
+            "per_m": per_m,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": launches}
+
+
+def bench_moe_sharded(args, fx, syn, dev, rank, world):
+    """Config 4, second part: the config-2 MoE layer expert-sharded over the ranks (rank g
+    holds experts [g*512/G, (g+1)*512/G) and the shared expert lives on rank 0); every rank
+    runs the routed GEMVs of its own experts into an fp32 partial [M, 2048], one NCCL SUM
+    all-reduce combines them and a bf16 rounding gives the layer output.  48 routings over
+    shifted expert sets are captured, collective included, in one CUDA graph per M; the
+    step time is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from flash_next_rtxpro6000_b200 import sharded
+
+    Ms = [int(m) for m in (args.ms or "16").split(",")]
+    if syn.EXPERTS % world:
+        raise SystemExit(f"{syn.EXPERTS} experts not divisible by {world} ranks")
+    E_local = syn.EXPERTS // world
+    e0 = rank * E_local
+    d, shared = _device_moe_layer(fx, syn, dev, seed=rank, experts=E_local)
+    if rank != 0:
+        shared = None
+    ws = fx.make_workspace(num_routes=syn.TOPK, hidden_size=syn.HIDDEN,
+                           intermediate_size=syn.INTER, device=dev)
+    peak, src = measured_peak()
+    sampler = ClockSampler(_gpu_id(dev)) if rank == 0 else None
+    clocks = None
+    n_rot = 48
+    per_m, total_bytes, total_ms, launches = {}, 0, 0.0, 0
+    for M in Ms:
+        rots, nbytes, local_bytes = [], 0, 0
+        for r in range(n_rot):
+            ids, wts = syn.routing(M, E=syn.EXPERTS, seed=1000 * M + r)
+            ids = ((ids.long() + 97 * r) % syn.EXPERTS).to(torch.int32)
+            uniq = torch.unique(ids)
+            nbytes += syn.moe_bytes(int(uniq.numel()), M=M)
+            mine = int(((uniq >= e0) & (uniq < e0 + E_local)).sum())
+            local_bytes += syn.moe_bytes(mine, M=M, shared=(rank == 0))
+            rots.append((ids.to(dev), wts.to(dev)))
+        x = syn.activations(M, seed=3).to(dev)
+        part = torch.empty(M, syn.HIDDEN, dtype=torch.float32, device=dev)
+        out = torch.empty(M, syn.HIDDEN, dtype=torch.bfloat16, device=dev)
+
+        def call(ids, wts):
+            fx.draft_moe_gemv(hidden_states=x, topk_ids=ids, topk_weights=wts,
+                              w13_weight=d["w13"], w13_blockscale_swizzled=d["s13"],
+                              w13_weight_scale_2=d["g13"], w2_weight=d["w2"],
+                              w2_blockscale_swizzled=d["s2"], w2_weight_scale_2=d["g2"],
+                              workspace=ws, shared_expert=shared, expert_offset=e0,
+                              out=part, out_f32=True, cfg=fx.DraftMoeGemvConfig(pdl=True))
+            dist.all_reduce(part, op=dist.ReduceOp.SUM)
+            out.copy_(part)
+
+        call(*rots[0])  # NCCL communicator up before the capture
+        torch.cuda.synchronize()
+        g = _graph_of([(lambda r=r: call(*r)) for r in rots])
+        reps = max(3, args.steps // n_rot)
+        ms, ck = _timed(g.replay, reps, 3, dev, world, sampler if M == Ms[-1] else None)
+        clocks = ck or clocks
+        us = ms / (reps * n_rot) * 1e3
+        per_m[str(M)] = {"us_per_call": round(us, 3),
+                         "GBps_aggregate": round(nbytes / n_rot / (us * 1e-6) / 1e9, 1),
+                         "bytes_per_call": int(nbytes / n_rot),
+                         "rank0_local_bytes_per_call": int(local_bytes / n_rot)}
+        total_bytes += nbytes * reps
+        total_ms += ms
+        launches += reps * n_rot * 3  # k1, k2, route sum (the NCCL sum and the bf16 copy
+        # are library kernels)
+        torch.cuda.synchronize()
+        del g
+    value = total_bytes / (total_ms / 1e3) / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
+                       "parallelism": f"expert-sharded x{world} ({E_local} experts per rank) + "
+                                      "NCCL SUM all-reduce of fp32 partials",
+                       "l2": f"{n_rot} routings over shifted expert sets in one CUDA graph"},
+            "per_m": per_m,
+            "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak,
+                         "unit": "GB/s per GPU", "frac": round(value / world / peak, 4),
+                         "traffic": None, "peak_source": src},
+            "clocks": clocks, "gpu_launches": launches}
 
 
 if __name__ == "__main__":

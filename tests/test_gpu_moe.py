@@ -196,3 +196,29 @@ def test_runner_maybe_apply_and_capture_guard():
     big = types.SimpleNamespace(hidden_states=torch.zeros(17, 2048, dtype=torch.bfloat16, device=dev()),
                                 hidden_states_scale=None, topk_output=disp.topk_output)
     assert runner.maybe_apply(layer=layer, dispatch_output=big) is None
+
+
+@pytest.mark.parametrize("out_f32", [False, True])
+def test_slice_without_routes_writes_zeros(out_f32):
+    """An expert-parallel slice that no route reaches (and no shared expert) still
+    writes its output: all zeros."""
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(64)
+    M = 4
+    x = syn.activations(M, seed=30).to(dev())
+    ids, wts = syn.routing(M, E=32, seed=30)  # every id in [0, 32)
+    ids, wts = ids.to(dev()), wts.to(dev())
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    out = torch.full((M, 2048), 7.0, dtype=torch.float32 if out_f32 else torch.bfloat16,
+                     device=dev())
+    sl = slice(32, 64)
+    fx.draft_moe_gemv(
+        hidden_states=x, topk_ids=ids, topk_weights=wts, w13_weight=d["w13"][sl].contiguous(),
+        w13_blockscale_swizzled=d["s13"][sl].contiguous(), w13_weight_scale_2=d["g13"][sl].contiguous(),
+        w2_weight=d["w2"][sl].contiguous(), w2_blockscale_swizzled=d["s2"][sl].contiguous(),
+        w2_weight_scale_2=d["g2"][sl].contiguous(), workspace=ws, expert_offset=32,
+        out=out, out_f32=out_f32)
+    torch.cuda.synchronize()
+    assert int(torch.count_nonzero(out)) == 0
