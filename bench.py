@@ -497,6 +497,7 @@ def bench_nvfp4(args, fx, syn, dev):
     per_m, total_bytes, total_ms = {}, 0, 0.0
     sampler = ClockSampler(_gpu_id(dev))
     clocks = None
+    launches = 0
     for M in Ms:
         x = syn.activations(M, seed=1).to(dev)
         y = torch.empty(M, syn.NVFP4_N, dtype=torch.bfloat16, device=dev)
@@ -512,6 +513,7 @@ def bench_nvfp4(args, fx, syn, dev):
         per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1)}
         total_bytes += b * reps * copies
         total_ms += ms
+        launches += reps * copies  # one GEMV launch per call
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
@@ -523,7 +525,7 @@ def bench_nvfp4(args, fx, syn, dev):
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": None}
+            "clocks": clocks, "gpu_launches": launches}
 
 
 def bench_norm_gated(args, fx, syn, dev):
@@ -544,6 +546,7 @@ def bench_norm_gated(args, fx, syn, dev):
     per_m, total_bytes, total_ms = {}, 0, 0.0
     sampler = ClockSampler(_gpu_id(dev))
     clocks = None
+    launches = 0  # both timed variants: one launch per call each
     for M in Ms:
         x = (torch.randn(M, K, generator=gen) * 0.5).bfloat16().to(dev)
         z = (torch.randn(M, K, generator=gen) * 0.5).bfloat16().to(dev)
@@ -558,6 +561,7 @@ def bench_norm_gated(args, fx, syn, dev):
                             sampler if (M == Ms[-1] and name == "norm") else None)
             clocks = ck or clocks
             res[name] = (ms, ms / (reps * copies) * 1e3)
+            launches += reps * copies
             del g
         b = N * K + 4 * N + 2 * G + 4 * M * K + 2 * M * N
         us = res["norm"][1]
@@ -575,7 +579,7 @@ def bench_norm_gated(args, fx, syn, dev):
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": None}
+            "clocks": clocks, "gpu_launches": launches}
 
 
 def bench_router(args, fx, syn, dev):
@@ -592,6 +596,7 @@ def bench_router(args, fx, syn, dev):
     per_m, total_bytes, total_ms = {}, 0, 0.0
     sampler = ClockSampler(_gpu_id(dev))
     clocks = None
+    launches = 0  # fused: one launch per call; unfused: router_gemv + softmax top-k
     for M in Ms:
         x = syn.activations(M, seed=1).to(dev)
         reps = max(3, args.steps // copies)
@@ -604,6 +609,7 @@ def bench_router(args, fx, syn, dev):
                             sampler if (M == Ms[-1] and name == "fused") else None)
             clocks = ck or clocks
             res[name] = (ms, ms / (reps * copies) * 1e3)
+            launches += reps * copies * (1 if name == "fused" else 2)
             del g
         b = 2 * E * K + 2 * M * K + 4 * M * E + 8 * M * k
         us = res["fused"][1]
@@ -621,7 +627,7 @@ def bench_router(args, fx, syn, dev):
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": None}
+            "clocks": clocks, "gpu_launches": launches}
 
 
 def bench_draft_step(args, fx, syn, dev):
@@ -641,6 +647,7 @@ def bench_draft_step(args, fx, syn, dev):
     per_m, total_bytes, total_ms = {}, 0, 0.0
     sampler = ClockSampler(_gpu_id(dev))
     clocks = None
+    launches = 0  # fused: one launch per call; unfused: GEMV + draft_topk1
     for M in Ms:
         x = syn.activations(M, seed=1).to(dev)
         pos = torch.zeros(M, dtype=torch.int64, device=dev)
@@ -659,6 +666,7 @@ def bench_draft_step(args, fx, syn, dev):
                             sampler if (M == Ms[-1] and name == "fused") else None)
             clocks = ck or clocks
             res[name] = (ms, ms / (reps * n) * 1e3)
+            launches += reps * n * (1 if name == "fused" else 2)
             del g
         b = syn.w8_head_bytes(V, K, M) + 8 * V  # + the token map
         us = res["fused"][1]
@@ -676,7 +684,7 @@ def bench_draft_step(args, fx, syn, dev):
             "per_m": per_m,
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": None}
+            "clocks": clocks, "gpu_launches": launches}
 
 
 def bench_moe(args, fx, syn, dev):
