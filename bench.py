@@ -1,10 +1,13 @@
 """Benchmark of the weight-only quantized GEMV hot path on B200.
 
-Default workload: the W8A16 lm_head GEMV with fused greedy argmax,
-int8 weights [151936, 2048] with per-row bf16 scales, one step = one call at each of
-M = 1, 4 and 16 tokens.  The weights (311 MB) exceed the 126 MB L2, so every call
-streams them from HBM.  Metric: HBM GB/s of algorithmic bytes (weights + scales +
-activations + logits + argmax), whole-job aggregate; µs per call is reported beside it.
+Default workload: the W8A16 lm_head GEMV with fused greedy argmax, int8 weights
+[151936, 2048] with per-row bf16 scales, one step = one call at each of M = 1, 4 and 16
+tokens.  The weights (311 MB) exceed the 126 MB L2, so every call streams them from HBM.
+Metric: HBM GB/s of algorithmic bytes (weights + scales + activations + logits +
+argmax), whole-job aggregate; µs per call is reported beside it.  The same run (one GPU)
+also measures the routed NVFP4 MoE layer (512 experts x 2048 x 512, top-10 + shared
+expert, M = 1 and 16) and the NVFP4 GEMV 4096 x 2048 (M = 1), each with its roofline
+and CPU baseline, under ``workloads`` in the one JSON line (``--no-extra`` skips them).
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
                     [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router|draft_step|stack]
@@ -51,6 +54,8 @@ def parse_args():
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
     ap.add_argument("--layers", type=int, default=48, help="MoE layers of --workload stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="default workload: skip the MoE and NVFP4 GEMV lines")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: greedy-key MAX inside the GEMV over NVLink (p2p) or by an "
@@ -137,71 +142,134 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU baseline
 def cpu_lm_head_sample(head_w, head_s, xs, rows: int, min_seconds: float):
-    """The reference's CPU path (dequantise then fp32 matmul, bf16 logits, argmax) on the
-    first `rows` rows, repeated for at least `min_seconds`.  Returns (GB/s, seconds, reps)."""
-    import numpy as np
-
+    """The reference's CPU path (dequantise then fp32 matmul, bf16 logits, argmax; torch on
+    all host threads) on the first `rows` rows, repeated for at least `min_seconds`.
+    Returns (GB/s, seconds, reps, cores)."""
     from flash_next_rtxpro6000_b200 import synthetic as syn
-    from oracle import w8a16 as ow8
+    from oracle import cpu_path
 
+    cores = _cpu_threads()
     w = head_w[:rows]
     s = head_s[:rows]
     K = w.shape[1]
     nbytes = sum(syn.w8_head_bytes(rows, K, x.shape[0]) for x in xs)
+    for x in xs:  # warm-up
+        cpu_path.lm_head_argmax(x, w, s)
     reps, t0 = 0, time.perf_counter()
     while True:
         for x in xs:
-            ow8.reference_cpu_path(x, w, "int8", s)
+            cpu_path.lm_head_argmax(x, w, s)
         reps += 1
         el = time.perf_counter() - t0
         if el >= min_seconds:
             break
-    return nbytes * reps / el / 1e9, el, reps
+    return nbytes * reps / el / 1e9, el, reps, cores
+
+
+def _cpu_threads():
+    import torch
+
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_nvfp4_sample(x, w, min_seconds: float):
+    """The reference's CPU path of config 0 (dequantise + fp32 matmul, torch, all cores),
+    repeated for at least min_seconds.  Returns (GB/s, seconds, calls, cores)."""
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+    from oracle import cpu_path
+
+    cores = _cpu_threads()
+    cpu_path.nvfp4_gemv(x, w.wq, w.bs, w.gscale)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_path.nvfp4_gemv(x, w.wq, w.bs, w.gscale)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    b = syn.nvfp4_bytes(w.wq.shape[0], 2 * w.wq.shape[1], x.shape[0])
+    return b * n / el / 1e9, el, n, cores
+
+
+def cpu_moe_sample(layer, x, ids, wts, nbytes: int, min_seconds: float):
+    """The reference's CPU path of config 2 (moe_reference restated in torch, all cores)
+    on one routing, repeated for at least min_seconds (at least one call).  Returns
+    (GB/s, seconds, calls, cores)."""
+    from oracle import cpu_path
+
+    cores = _cpu_threads()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_path.moe_layer(x, ids, wts, layer)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return nbytes * n / el / 1e9, el, n, cores
 
 
 def run_reference(args):
-    """--impl reference: time the reference's CPU path (restated in numpy) on rank 0."""
+    """--impl reference: the reference's CPU path (torch dequantise-then-matmul, restated
+    in oracle/cpu_path.py because the reference's source does not travel to the GPU box),
+    on rank 0 with all host threads; the other ranks exit without work.  Each step is a
+    bounded sample of the default workload: the first 16,384 of the lm_head's rows at
+    every M.  The same run samples the MoE layer and the NVFP4 GEMV (``workloads``)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
     import torch
 
     from flash_next_rtxpro6000_b200 import synthetic as syn
+    from oracle import cpu_path
 
+    cores = _cpu_threads()
     Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
     V = syn.VOCAB if args.workload != "draft_head" else syn.DRAFT_VOCAB
-    rows = 1024
+    rows = 16384
     head = syn.w8_head(rows, syn.HIDDEN, seed=0)
-    w = head.w.numpy()
-    s = head.scale.float().numpy()
-    xs = [syn.activations(m, seed=1).float().numpy() for m in Ms]
-    from oracle import w8a16 as ow8
-
+    xs = [syn.activations(m, seed=1) for m in Ms]
     step_bytes = sum(syn.w8_head_bytes(rows, syn.HIDDEN, m) for m in Ms)
     for _ in range(max(1, args.warmup)):
         for x in xs:
-            ow8.reference_cpu_path(x, w, "int8", s)
+            cpu_path.lm_head_argmax(x, head.w, head.scale)
+    steps = max(1, min(args.steps, 200))
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         for x in xs:
-            ow8.reference_cpu_path(x, w, "int8", s)
+            cpu_path.lm_head_argmax(x, head.w, head.scale)
     el = time.perf_counter() - t0
-    value = step_bytes * args.steps / el / 1e9
-    cores = os.cpu_count()
-    sample = (f"first {rows} of {V} rows of the int8 lm_head, M={Ms}, per step; numpy fp32 "
+    value = step_bytes * steps / el / 1e9
+    sample = (f"first {rows} of {V} rows of the int8 lm_head, M={Ms}, per step; torch fp32 "
               "dequantise + matmul + bf16 round + argmax")
-    print(json.dumps({
+    res = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(el / steps * 1e3, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8/bf16", "data": "synthetic",
         "config": {"workload": f"w8a16_{args.workload}_{V}x{syn.HIDDEN}_argmax", "M": Ms},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }
+    if args.workload == "lm_head" and not args.no_extra:
+        w0 = syn.nvfp4_weight(syn.NVFP4_N, syn.HIDDEN, seed=0)
+        gbs, el0, n0, _ = cpu_nvfp4_sample(syn.activations(1, seed=1), w0, min_seconds=3.0)
+        L = syn.moe_layer(syn.EXPERTS, syn.HIDDEN, syn.INTER, seed=0)
+        moe = {}
+        for M in (1, 16):
+            ids, wts = syn.routing(M, E=syn.EXPERTS, seed=1000 * M)
+            b = syn.moe_bytes(int(torch.unique(ids).numel()), M=M)
+            g, e, n, _ = cpu_moe_sample(L, syn.activations(M, seed=3), ids, wts, b, 2.0)
+            moe[str(M)] = {"value": round(g, 4), "calls": n, "seconds": round(e, 2)}
+        res["workloads"] = {
+            "nvfp4": {"config": {"workload": "nvfp4_gemv_4096x2048", "M": [1]},
+                      "value": round(gbs, 3), "sample": f"{n0} calls in {el0:.1f} s"},
+            "moe": {"config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": [1, 16]},
+                    "per_m": moe}}
+    print(json.dumps(res), flush=True)
 
 
 # ------------------------------------------------------------------ our arm
@@ -231,6 +299,8 @@ def main():
 
     if args.workload in ("lm_head", "draft_head"):
         res = bench_lm_head(args, fx, syn, dev, rank, world)
+        if args.workload == "lm_head" and world == 1 and not args.no_extra:
+            res["workloads"] = extra_workloads(args, fx, syn, dev)
     elif args.workload == "nvfp4":
         res = bench_nvfp4(args, fx, syn, dev)
     elif args.workload == "norm_gated":
@@ -409,16 +479,31 @@ def bench_lm_head(args, fx, syn, dev, rank, world):
     if ex is not None:
         ex.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import numpy as np
-
-        xs_np = [x.float().cpu().numpy() for x in xs]
-        gbs, el, reps = cpu_lm_head_sample(head.w.numpy(), head.scale.float().numpy(), xs_np,
-                                           rows=16384, min_seconds=10.0)
-        res["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": os.cpu_count(),
+        gbs, el, reps, cores = cpu_lm_head_sample(head.w, head.scale, [x.cpu() for x in xs],
+                                                  rows=16384, min_seconds=10.0)
+        res["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": cores,
                                "kind": "port",
                                "sample": f"16384 of {V} rows, M={Ms}, {reps} reps in {el:.1f} s "
-                                         "(numpy fp32 dequantise+matmul, bf16 round, argmax)"}
+                                         "(torch fp32 dequantise+matmul, bf16 round, argmax, "
+                                         "all host threads)"}
     return res
+
+
+def extra_workloads(args, fx, syn, dev):
+    """The MoE layer (M = 1, 16) and the NVFP4 GEMV (M = 1) of the default run."""
+    import copy
+
+    out = {}
+    a = copy.copy(args)
+    a.ms = "1,16"
+    out["moe"] = bench_moe(a, fx, syn, dev, cpu=not args.no_cpu_baseline)
+    a.ms = "1"
+    out["nvfp4"] = bench_nvfp4(a, fx, syn, dev, cpu=not args.no_cpu_baseline)
+    for k in ("metric", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "data"):
+        for v in out.values():
+            v.pop(k, None)
+    return out
 
 
 def _lib_handle():
@@ -484,15 +569,35 @@ def _graph_of(calls, warm=3):
     return g
 
 
-def bench_nvfp4(args, fx, syn, dev):
+def _roofline_per_m(per_m, peak, src, kernel, traffic_key=None):
+    """Roofline object of a workload measured at several M: achieved = total algorithmic
+    bytes / total launch time over the M values; per-M achieved / frac beside it;
+    traffic = ncu DRAM bytes per launch from profiles/ (averaged over the M values
+    captured), or None."""
+    tot_b = sum(v["bytes_per_call"] for v in per_m.values())
+    tot_us = sum(v["us_per_call"] for v in per_m.values())
+    ach = tot_b / (tot_us * 1e-6) / 1e9
+    tr = traffic_for(traffic_key) if traffic_key else None
+    traffic = None
+    if tr:
+        got = [tr[m] for m in per_m if m in tr]
+        traffic = round(sum(got) / len(got)) if got else None
+    return {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(ach / peak, 4), "traffic": traffic, "peak_source": src,
+            "kernel": kernel, "bytes_per_launch_avg": tot_b // len(per_m),
+            "per_m": {m: {"achieved": v["GBps"], "frac": round(v["GBps"] / peak, 4)}
+                      for m, v in per_m.items()}}
+
+
+def bench_nvfp4(args, fx, syn, dev, cpu=False):
     """Config 0 (NVFP4 4096 x 2048): 64 weight copies rotated (> 4x L2) inside one CUDA
     graph, so the timing is device time, not Python dispatch."""
     import torch
 
     Ms = [int(m) for m in (args.ms or "1,4,16").split(",")]
     copies = 64
-    ws = [syn.nvfp4_weight(syn.NVFP4_N, syn.HIDDEN, seed=i) for i in range(copies)]
-    ws = [(w.wq.to(dev), w.bs.to(dev), w.gscale.to(dev)) for w in ws]
+    host = [syn.nvfp4_weight(syn.NVFP4_N, syn.HIDDEN, seed=i) for i in range(copies)]
+    ws = [(w.wq.to(dev), w.bs.to(dev), w.gscale.to(dev)) for w in host]
     peak, src = measured_peak()
     per_m, total_bytes, total_ms = {}, 0, 0.0
     sampler = ClockSampler(_gpu_id(dev))
@@ -510,22 +615,31 @@ def bench_nvfp4(args, fx, syn, dev):
         clocks = ck or clocks
         us = ms / (reps * copies) * 1e3
         b = syn.nvfp4_bytes(syn.NVFP4_N, syn.HIDDEN, M)
-        per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1)}
+        per_m[str(M)] = {"us_per_call": round(us, 3), "GBps": round(b / (us * 1e-6) / 1e9, 1),
+                         "bytes_per_call": b}
         total_bytes += b * reps * copies
         total_ms += ms
         launches += reps * copies  # one GEMV launch per call
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9
-    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": "nvfp4_gemv_4096x2048", "M": Ms,
-                       "l2": f"{copies} weight copies rotated in one CUDA graph (> 4x L2)"},
-            "per_m": per_m,
-            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": launches}
+    res = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
+           "config": {"workload": "nvfp4_gemv_4096x2048", "M": Ms,
+                      "l2": f"{copies} weight copies rotated in one CUDA graph (> 4x L2)"},
+           "per_m": per_m,
+           "roofline": _roofline_per_m(per_m, peak, src, "dense_gemv_kernel<nvfp4>",
+                                       "dense_gemv_nvfp4_config0"),
+           "clocks": clocks, "gpu_launches": launches}
+    if cpu:
+        x = syn.activations(Ms[0], seed=1)
+        gbs, el, n, cores = cpu_nvfp4_sample(x, host[0], min_seconds=3.0)
+        res["cpu_baseline"] = {"value": round(gbs, 3), "unit": UNIT, "cores": cores,
+                               "kind": "port",
+                               "sample": f"M={Ms[0]}, {n} calls in {el:.1f} s (torch fp32 "
+                                         "dequantise + matmul, bf16 out, all host threads)"}
+    return res
 
 
 def bench_norm_gated(args, fx, syn, dev):
@@ -687,7 +801,7 @@ def bench_draft_step(args, fx, syn, dev):
             "clocks": clocks, "gpu_launches": launches}
 
 
-def bench_moe(args, fx, syn, dev):
+def bench_moe(args, fx, syn, dev, cpu=False):
     """Config 2 (NVFP4 MoE, 512 experts, top-10 + shared expert).  48 routings rotate over
     shifted expert sets (> 4x L2 across the rotation) inside one CUDA graph."""
     import torch
@@ -710,6 +824,7 @@ def bench_moe(args, fx, syn, dev):
     clocks = None
     n_rot = 48
     launches = 0
+    first_routing = {}
     for M in Ms:
         rots, nbytes = [], 0
         for r in range(n_rot):
@@ -719,6 +834,8 @@ def bench_moe(args, fx, syn, dev):
             ids = ((ids.long() + 97 * r) % syn.EXPERTS).to(torch.int32)
             nbytes += syn.moe_bytes(int(torch.unique(ids).numel()), M=M)
             rots.append((ids.to(dev), wts.to(dev)))
+            if r == 0:
+                first_routing[M] = (ids, wts)
         x = syn.activations(M, seed=3).to(dev)
         out = torch.empty(M, syn.HIDDEN, dtype=torch.bfloat16, device=dev)
 
@@ -741,19 +858,36 @@ def bench_moe(args, fx, syn, dev):
                            "bytes_per_call": int(bytes_per_call)}
         total_bytes += bytes_per_call * reps * n_rot
         total_ms += ms
-        launches += reps * n_rot * 3  # k1, k2, route sum
+        launches += reps * n_rot * fx.moe_launches_per_call(M, syn.TOPK, syn.EXPERTS,
+                                                             syn.HIDDEN, syn.INTER)
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9
-    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
-                       "l2": f"{n_rot} routings over shifted expert sets in one CUDA graph (> 4x L2)"},
-            "per_m": results,
-            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(value / peak, 4), "traffic": None, "peak_source": src},
-            "clocks": clocks, "gpu_launches": launches}
+    res = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "nvfp4/bf16 (fp32 accumulate)", "data": "synthetic",
+           "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
+                      "l2": f"{n_rot} routings over shifted expert sets in one CUDA graph (> 4x L2)"},
+           "per_m": results,
+           "roofline": _roofline_per_m(results, peak, src, fx.moe_kernel_name(Ms[0]),
+                                       "moe_nvfp4_config2"),
+           "clocks": clocks, "gpu_launches": launches}
+    if cpu:
+        cb = {}
+        for M in Ms:
+            ids, wts = first_routing[M]
+            b = syn.moe_bytes(int(torch.unique(ids).numel()), M=M)
+            gbs, el, n, cores = cpu_moe_sample(L, syn.activations(M, seed=3), ids, wts, b,
+                                               min_seconds=2.0)
+            cb[str(M)] = {"value": round(gbs, 4), "calls": n, "seconds": round(el, 2)}
+        tot = sum(results[m]["bytes_per_call"] for m in cb)
+        sec = sum(cb[m]["seconds"] / cb[m]["calls"] for m in cb)
+        res["cpu_baseline"] = {"value": round(tot / sec / 1e9, 4), "unit": UNIT, "cores": cores,
+                               "kind": "port", "per_m": cb,
+                               "sample": "one routing per M, whole layer (torch moe_reference "
+                                         "restated: per route dequantise + gate/up + silu*up "
+                                         "+ down, fp32, all host threads)"}
+    return res
 
 
 def _device_moe_layer(fx, syn, dev, seed, experts=None):

@@ -15,7 +15,9 @@ the hand-written CUDA library ``_fnx.so``):
   hot-vocabulary token map (the latter fused into the draft head's argmax);
 * ``nvfp4_dense`` -- the NVFP4 dense lm_head: load-time packing with an on-disk cache
   and the linear method serving it through the NVFP4 GEMV;
-* ``sharded`` -- vocab-sharded lm_head and expert-sharded MoE over torch.distributed.
+* ``sharded`` -- vocab-sharded lm_head and expert-sharded MoE over torch.distributed;
+* ``check_device_errors`` -- reads (and clears) the error flags that the kernels' bounded
+  waits set when they run out of time.
 """
 
 from .w8a16_gemv import (  # noqa: F401
@@ -44,9 +46,12 @@ from .draft_moe_gemv import (  # noqa: F401
     enable_draft_moe_gemv,
     make_workspace,
     moe_gemv,
+    moe_kernel_name,
+    moe_launches_per_call,
     unsupported_reason,
 )
 
+from .errors import DeviceWaitError, check_device_errors  # noqa: F401
 from .router import covered, route_softmax_fast, router_gemv, router_topk  # noqa: F401
 from .draft_topk1 import draft_head_topk1, draft_topk1_postprocess  # noqa: F401
 

@@ -18,6 +18,19 @@ SCALE_NONE, SCALE_F32_SCALAR, SCALE_F32_ROW, SCALE_BF16_SCALAR, SCALE_BF16_ROW =
 MAX_M = 16
 STATIC_PARTIAL_FLOATS, STATIC_COUNTERS = 256 * 1024, 2048  # fnx_w8a16_gemv_static_ws limits
 PEER_BUFFER_BYTES, IPC_HANDLE_BYTES, MAX_PEERS = 4096, 64, 8
+# device error codes (FNX_DEVERR_* in include/fnx_gemv.h)
+DEVICE_ERRORS = {
+    1: "WAIT_FULL: a consumer waited for a weight stage",
+    2: "WAIT_EMPTY: the producer waited for a free stage",
+    3: "WAIT_RED: an epilogue waited for consumer partials",
+    4: "WAIT_RFREE: a consumer waited for a free reduction slot",
+    5: "DRAIN: in-flight copies did not land before exit",
+    6: "WAIT_X: the activation rows did not arrive",
+    7: "WAIT_PEER: another rank did not publish its greedy key",
+    8: "PEER_DESYNC: another rank is two or more calls ahead",
+    9: "ROUTES: a routing table the kernel cannot hold",
+    10: "WAIT_EXPERT: a down projection waited for its expert's activations",
+}
 
 EXPORTED = (
     "fnx_plan_gemv",
@@ -36,11 +49,13 @@ EXPORTED = (
     "fnx_ipc_open",
     "fnx_ipc_close",
     "fnx_peer_setup",
+    "fnx_peer_set_wait_limit",
     "fnx_w8a16_gemv_vocab_sharded",
     "fnx_w4a16_nvfp4_gemv",
     "fnx_moe_workspace_bytes",
     "fnx_moe_gemv",
     "fnx_argmax_decode",
+    "fnx_static_ws_error",
     "fnx_last_error",
     "fnx_version",
 )
@@ -159,6 +174,8 @@ def _declare(lib):
         _P, c_int64, _P, _P, c_int, c_int, POINTER(FnxMoeWeights), POINTER(FnxMoeWeights), _P,
         c_int64, c_int, POINTER(FnxMoeWorkspace), c_int, _P]
     lib.fnx_argmax_decode.argtypes = [_P, _P, c_int, _P]
+    lib.fnx_peer_set_wait_limit.argtypes = [_P, c_int64]
+    lib.fnx_static_ws_error.argtypes = [c_int, _P, POINTER(c_int)]
     lib.fnx_last_error.restype = c_char_p
     lib.fnx_version.restype = c_char_p
     for name in EXPORTED:

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <cstring>
 #include <cstdarg>
 #include <cstdio>
@@ -455,7 +456,7 @@ int moe_geometry(int M, int R, int E, int H, int I, MoeGeo& g) {
 // For them the scratch lives in one static array per device, laid out as
 //   [0, 128)      argmax keys (16 x u64)        cleared before each launch
 //   [256, 260)    argmax counter (u32)          cleared before each launch
-//   [512, 516)    device error word (i32)
+//   [512, 516)    device error word (i32)       cleared before each launch
 //   [4096, ...)   split-K counters (the ones a launch uses are cleared before it), then
 //                 split-K partial floats
 static __device__ __align__(256) unsigned char g_static_scratch[FNX_STATIC_SCRATCH_BYTES];
@@ -561,16 +562,36 @@ int fnx_w8a16_gemv_static_ws(const void* x, int64_t ldx, const void* w, int64_t 
   ws.partials = reinterpret_cast<float*>(b + 4096 + 4 * FNX_STATIC_COUNTERS);
   ws.partial_floats = FNX_STATIC_PARTIAL_FLOATS;
   // The array keeps whatever the previous call left; a call that ended early (a wait
-  // that gave up) may have left keys or counters set.  Clear what this launch needs at
-  // zero, on the caller's stream, before it runs (a memset allocates nothing).
+  // that gave up) may have left keys or counters set, or the error word.  Clear what this
+  // launch needs at zero, on the caller's stream, before it runs (one contiguous memset of
+  // keys, counter and error word; a memset allocates nothing).
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(b, 0, 260, st) != cudaSuccess ||
+  if (cudaMemsetAsync(b, 0, 516, st) != cudaSuccess ||
       (counters > 0 && cudaMemsetAsync(b + 4096, 0, (size_t)counters * 4, st) != cudaSuccess))
     return cuda_fail("clearing the static scratch");
   DenseCall c = {x, ldx, w, ldw, w_dtype, nullptr, 0, scale, scale_kind, y, ldy, y2, ldy2,
                  split_n, out_f32, argmax_out, argmax_key_out, row_offset, M, N, K, 0,
                  cfg, &ws, pdl, static_cast<cudaStream_t>(stream)};
   return run_dense(c);
+}
+
+int fnx_static_ws_error(int clear, fnx_stream_t stream, int* code) {
+  g_err.clear();
+  if (!code) return fail(FNX_EINVAL, "null code");
+  void* base = nullptr;
+  if (int rc = static_scratch(&base)) return rc;
+  int* word = reinterpret_cast<int*>(static_cast<unsigned char*>(base) + 512);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  if (cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return cuda_fail("reading the static scratch's error word");
+  if (clear && v != 0 &&
+      (cudaMemsetAsync(word, 0, sizeof(int), st) != cudaSuccess ||
+       cudaStreamSynchronize(st) != cudaSuccess))
+    return cuda_fail("clearing the static scratch's error word");
+  *code = v;
+  return FNX_OK;
 }
 
 int fnx_w8a16_gemv_silu_mul(const void* x, int64_t ldx, const void* w, int64_t ldw,
@@ -847,6 +868,17 @@ int fnx_peer_setup(void* local, void* const* bufs, int world, int rank) {
   if (cudaMemcpy(static_cast<unsigned char*>(local) + fnx::kPeerDescOff, &d, sizeof(d),
                  cudaMemcpyHostToDevice) != cudaSuccess)
     return cuda_fail("writing the peer table");
+  return FNX_OK;
+}
+
+int fnx_peer_set_wait_limit(void* local, int64_t wait_ns) {
+  g_err.clear();
+  if (!local || wait_ns < 0) return fail(FNX_EINVAL, "null buffer or negative limit");
+  const unsigned long long v = (unsigned long long)wait_ns;
+  if (cudaMemcpy(static_cast<unsigned char*>(local) + fnx::kPeerDescOff +
+                     offsetof(fnx::PeerDesc, wait_ns),
+                 &v, sizeof(v), cudaMemcpyHostToDevice) != cudaSuccess)
+    return cuda_fail("writing the wait limit");
   return FNX_OK;
 }
 

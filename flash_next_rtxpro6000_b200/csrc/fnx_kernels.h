@@ -55,6 +55,7 @@ constexpr int kPeerFlagsOff = 2048, kPeerEpochOff = 2560, kPeerDescOff = 2624;
 struct PeerDesc {
   unsigned char* buf[8];
   int world, rank;
+  unsigned long long wait_ns;  // limit of the wait for the other ranks (0: kWaitLimitNs)
 };
 
 // The exchange step, done by one warp of the last CTA: lane m < M holds this rank's key of
@@ -62,22 +63,26 @@ struct PeerDesc {
 // its key into every rank's buffer (slot of this call's epoch parity), fences at system
 // scope once and writes the epoch into every rank's flag of (this rank, token m) (a
 // release pattern: the fence orders its key stores before the flags); it then polls its
-// own buffer's flags of token m with acquire loads until every rank has published at
-// least this epoch, and reads the keys.  No cross-lane ordering is needed: each lane pairs
-// its own stores and loads.  A rank can run at most one call ahead of another (it needs the
-// other's flags to finish a call), so two key slots suffice.  An expired wait (2 s)
-// records ERR_WAIT_PEER and returns this rank's own key.
+// own buffer's flags of token m with acquire loads until every rank has published this
+// epoch or the next one, and reads the keys.  No cross-lane ordering is needed: each lane
+// pairs its own stores and loads.  In step, a rank can run at most one call ahead of
+// another (it needs the other's flags to finish a call), so two key slots suffice.
+// Failures keep this rank's own key and record an error code:
+//  * ERR_WAIT_PEER: a rank did not publish within the wait limit (2 s by default);
+//  * ERR_PEER_DESYNC: a rank is two or more calls ahead (the ranks' call sequences
+//    diverged, e.g. after an expired wait), so its key slot may hold a later call's key.
 static __device__ __noinline__ unsigned long long peer_key_max(unsigned char* pbuf,
                                                                unsigned long long key, int M,
                                                                int* err) {
   const int lane = threadIdx.x & 31;
   const PeerDesc* d = reinterpret_cast<const PeerDesc*>(pbuf + kPeerDescOff);
   const int world = d->world, rank = d->rank;
+  const unsigned long long limit = d->wait_ns ? d->wait_ns : kWaitLimitNs;
   unsigned* epoch_p = reinterpret_cast<unsigned*>(pbuf + kPeerEpochOff);
   const unsigned e = *epoch_p + 1u;
   const int par = e & 1u;
   unsigned long long best = key;
-  bool ok = true;
+  bool ok = true, desync = false;
   if (lane < M) {
     for (int r = 0; r < world; ++r) {
       unsigned long long* dst =
@@ -98,8 +103,14 @@ static __device__ __noinline__ unsigned long long peer_key_max(unsigned char* pb
       for (;;) {
         unsigned v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-        if ((int)(v - e) >= 0) break;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        const int ahead = (int)(v - e);
+        if (ahead >= 2) {
+          ok = false;
+          desync = true;
+          break;
+        }
+        if (ahead >= 0) break;
+        if (global_ns() - t0 > limit) {
           ok = false;
           break;
         }
@@ -115,7 +126,9 @@ static __device__ __noinline__ unsigned long long peer_key_max(unsigned char* pb
     }
     if (!ok) best = key;
   }
-  if (!__all_sync(0xffffffffu, ok) && lane == 0) record_error(err, ERR_WAIT_PEER);
+  const bool any_desync = __any_sync(0xffffffffu, desync);
+  if (!__all_sync(0xffffffffu, ok) && lane == 0)
+    record_error(err, any_desync ? ERR_PEER_DESYNC : ERR_WAIT_PEER);
   if (lane == 0) *epoch_p = e;
   return best;
 }

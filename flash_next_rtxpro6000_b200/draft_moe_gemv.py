@@ -24,7 +24,7 @@ from typing import Optional
 
 import torch
 
-from . import _lib
+from . import _lib, errors
 from ._lib import FnxMoeWeights, FnxMoeWorkspace, FnxMoeWorkspaceSizes, check, ptr
 from .w8a16_gemv import _activation, _stream
 
@@ -116,12 +116,14 @@ def make_workspace(*, num_routes: int, hidden_size: int, intermediate_size: int,
           "make_workspace")
     pairs = m * (num_routes + 1)
     u8 = dict(dtype=torch.uint8, device=device)
-    return DraftMoeWorkspace(
+    ws = DraftMoeWorkspace(
         act=torch.empty(sz.act, **u8),
         partials=torch.empty((pairs, hidden_size), dtype=torch.float32, device=device),
         error_flag=torch.zeros(1, dtype=torch.int32, device=device),
         max_tokens=m, num_routes=num_routes,
     )
+    errors.register(ws.error_flag, f"MoE workspace ({m} tokens x {num_routes} routes) on {device}")
+    return ws
 
 
 def _u8(t: torch.Tensor) -> torch.Tensor:
@@ -206,6 +208,17 @@ def draft_moe_gemv(
 
 #: The M <= 16 entry point under a width-neutral name.
 moe_gemv = draft_moe_gemv
+
+
+def moe_launches_per_call(M: int, num_routes: int, num_experts: int, hidden_size: int,
+                          intermediate_size: int) -> int:
+    """Kernel launches one draft_moe_gemv call makes for these shapes."""
+    return 3
+
+
+def moe_kernel_name(M: int) -> str:
+    """The kernel(s) one draft_moe_gemv call runs."""
+    return "moe_up_kernel + moe_down_kernel + moe_sum_kernel"
 
 
 def _is_small_batch_call(dispatch_output, max_tokens: int = 16) -> bool:

@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from ._lib import check, ptr
-from .w8a16_gemv import (PDL, _activation, _cfg, _out_or_new, _scale_kind, _stream,
+from .w8a16_gemv import (PDL, _activation, _cfg, _k_major, _out_or_new, _scale_kind, _stream,
                          _weight_kind, _workspace)
 
 
@@ -97,8 +97,7 @@ def draft_head_topk1(
     M, K = x.shape
     N = w.shape[0]
     assert w.shape[1] == K and M <= 16
-    if w.stride(1) != 1:
-        raise ValueError("the draft head needs a K-contiguous [N, K] weight")
+    _k_major(w, "draft_head_topk1")
     _check_chain(M, N, x.device, positions, draft_tokens, draft_token_column, hot_token_id)
     y = _out_or_new(out, M, N, x.device)
     x = _activation(x)

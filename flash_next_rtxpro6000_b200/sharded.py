@@ -24,7 +24,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
-from . import _lib
+from . import _lib, errors
 from ._lib import check, ptr
 from .draft_moe_gemv import DraftMoeWorkspace, SharedExpert, draft_moe_gemv
 from .w8a16_gemv import PDL, _activation, _scale_kind, _stream, _weight_kind, _workspace
@@ -116,6 +116,11 @@ class PeerExchange:
         if multi:
             dist.barrier(group=group)
 
+    def set_wait_limit(self, seconds: float) -> None:
+        """Limit of each call's wait for the other ranks' keys (default 2 s)."""
+        check(_lib.lib().fnx_peer_set_wait_limit(self.buf, int(seconds * 1e9)),
+              "fnx_peer_set_wait_limit")
+
     def close(self):
         """Unmap the other ranks' buffers and free this rank's (after every rank's last
         call has finished)."""
@@ -133,9 +138,17 @@ class PeerExchange:
 
 
 def vocab_sharded_lm_head(x, w_shard, s_shard, row_offset: int, exchange: PeerExchange,
-                          out=None, argmax_out=None, pdl: Optional[bool] = True):
+                          out=None, argmax_out=None, pdl: Optional[bool] = True,
+                          check_errors: bool = False):
     """Greedy token of a vocab-sharded head in one launch per rank: the shard's GEMV with
-    the MAX over ranks of the greedy keys done by its last CTA over NVLink (no NCCL)."""
+    the MAX over ranks of the greedy keys done by its last CTA over NVLink (no NCCL).
+
+    If another rank does not publish its key within the exchange's wait limit (2 s by
+    default, ``PeerExchange.set_wait_limit``), or is two or more calls ahead, this rank
+    keeps its own shard's token and the GEMV scratch's error flag is set: ``argmax_out``
+    is then not the global greedy token.  ``check_errors=True`` synchronises the stream after the
+    call, clears the flag and raises ``errors.DeviceWaitError`` when it was set (outside
+    graph capture only); otherwise ``errors.check_device_errors()`` reports it later."""
     M, K = x.shape
     N = w_shard.shape[0]
     x = _activation(x)
@@ -149,6 +162,8 @@ def vocab_sharded_lm_head(x, w_shard, s_shard, row_offset: int, exchange: PeerEx
         ptr(am), row_offset, M, N, K, exchange.buf, None, ctypes.byref(ws.c),
         int(PDL if pdl is None else pdl), _stream(x))
     check(rc, "vocab_sharded_lm_head")
+    if check_errors:
+        errors.check_flag(ws.error_flag, "vocab_sharded_lm_head")
     return y, am
 
 

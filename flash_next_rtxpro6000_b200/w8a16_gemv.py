@@ -14,14 +14,17 @@ greedy top-1 of the bf16-rounded logits (lowest row on ties) into the same launc
 
 from __future__ import annotations
 
+import logging
 import os
 from dataclasses import dataclass
 from typing import Optional, Tuple, Union
 
 import torch
 
-from . import _lib
+from . import _lib, errors
 from ._lib import FnxGemvCfg, FnxWorkspace, check, ptr
+
+logger = logging.getLogger(__name__)
 
 # Split-K scratch sizes (the reference's w8a16_gemv.py:329-331).
 _WS_FLOATS = 1 << 21
@@ -69,6 +72,7 @@ class Workspace:
         self.argmax_keys = torch.zeros(_lib.MAX_M, dtype=torch.int64, device=device)
         self.argmax_count = torch.zeros(1, dtype=torch.int32, device=device)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=device)
+        errors.register(self.error_flag, f"dense GEMV scratch on {device}")
         self.c = FnxWorkspace(ptr(self.partials), _WS_FLOATS, ptr(self.counters), _WS_COUNTERS,
                               ptr(self.argmax_keys), ptr(self.argmax_count),
                               ptr(self.error_flag))
@@ -194,15 +198,40 @@ def _scale_kind(s: torch.Tensor, N: int) -> Tuple[torch.Tensor, int]:
     return s, _lib.SCALE_F32_ROW if s.dtype == torch.float32 else _lib.SCALE_BF16_ROW
 
 
+_REF_CFG_NOTED = [False]
+
+
 def _cfg(cfg) -> Optional[FnxGemvCfg]:
-    """Our geometry (GemvConfig or its 5-tuple); None = planner."""
+    """Our geometry (GemvConfig or its 2..5-tuple); None = planner.
+
+    The reference's own 7-tuple ``(BLOCK_N, BLOCK_K, SPLITS, use_dot, w_kn, warps,
+    stages)`` (w8a16_gemv.py:522-538) describes a Triton tiling with no counterpart in
+    this kernel; it is accepted and ignored (the planner chooses), noted once in the log.
+    """
     if cfg is None:
         return None
     if isinstance(cfg, GemvConfig):
         return cfg.to_c()
+    if isinstance(cfg, (tuple, list)) and len(cfg) == 7:
+        if not _REF_CFG_NOTED[0]:
+            logger.info("w8a16 gemv: ignoring the Triton tile config %r; this library plans "
+                        "its own launch geometry", tuple(cfg))
+            _REF_CFG_NOTED[0] = True
+        return None
     if isinstance(cfg, (tuple, list)) and len(cfg) in (2, 3, 4, 5):
         return GemvConfig(*cfg).to_c()
-    raise ValueError(f"cfg must be a GemvConfig or (warps, chunks_per_warp[, groups, ksplit, grid]); got {cfg!r}")
+    raise ValueError(f"cfg must be a GemvConfig, (warps, chunks_per_warp[, groups, ksplit, "
+                     f"grid]) or the reference's 7-tuple; got {cfg!r}")
+
+
+def _k_major(w: torch.Tensor, what: str) -> None:
+    """The kernels stream K-contiguous weight rows.  An N-contiguous view (the reference's
+    W_KN case, w8a16_gemv.py:586) is declined with NotImplementedError, like every other
+    shape this library does not tile, so the caller keeps its own path."""
+    if w.stride(1) != 1:
+        raise NotImplementedError(
+            f"{what}: only K-contiguous [N, K] weights (stride(1) == 1) are supported; got "
+            f"strides {tuple(w.stride())}")
 
 
 def _argmax_dest(argmax_out, M: int, device):
@@ -234,8 +263,7 @@ def w8a16_gemv(
     N = w.shape[0]
     assert w.shape[1] == K and M <= 16
     y, y2, split_n = _split_dests(out, out2, split_n, M, N, x.device)
-    if w.stride(1) != 1:
-        raise ValueError("w8a16 gemv needs a K-contiguous [N, K] weight (stride(1) == 1)")
+    _k_major(w, "w8a16_gemv")
     x = _activation(x)
     s, skind = _scale_kind(scale, N)
     am = _argmax_dest(argmax_out, M, x.device)
@@ -284,8 +312,7 @@ def w8a16_gemv_silu_mul(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, c
         raise ValueError(f"out= must be a row-contiguous bf16 [{M}, {H}] tensor")
     s, skind = _scale_kind(scale, N)
     assert s.numel() == N, "fused gate_up needs a per-channel scale"
-    if w.stride(1) != 1:
-        raise ValueError("fused gate_up needs a K-contiguous weight")
+    _k_major(w, "w8a16_gemv_silu_mul")
     x = _activation(x)
     ws = _workspace(x.device)
     c = _cfg(cfg)
@@ -384,8 +411,7 @@ def w8a16_gemv_norm_gated(
     if norm_weight.dtype not in (torch.bfloat16, torch.float32) or \
             norm_weight.numel() != group_size:
         raise ValueError(f"norm_weight must be a bf16/fp32 [{group_size}] vector")
-    if w.stride(1) != 1:
-        raise ValueError("w8a16 gemv needs a K-contiguous [N, K] weight (stride(1) == 1)")
+    _k_major(w, "w8a16_gemv_norm_gated")
     y = _out_or_new(out, M, N, x.device)
     x = _activation(x)
     z = _activation(z)

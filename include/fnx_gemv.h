@@ -73,6 +73,21 @@ typedef void* fnx_stream_t;
 /* Maximum tokens per call (the reference asserts M <= 16, w8a16_gemv.py:658). */
 #define FNX_MAX_M 16
 
+/* Device error codes.  A device-side wait that runs out of time (2 s unless stated
+ * otherwise) records the first such code of a call in the workspace's error_flag, leaves
+ * its loop, and the launch completes with wrong results; the host reads the flag (after
+ * the work has finished) and clears it.  Nothing on the device clears it. */
+#define FNX_DEVERR_WAIT_FULL 1     /* a consumer waited for a weight stage          */
+#define FNX_DEVERR_WAIT_EMPTY 2    /* the producer waited for a free stage          */
+#define FNX_DEVERR_WAIT_RED 3      /* an epilogue waited for consumer partials      */
+#define FNX_DEVERR_WAIT_RFREE 4    /* a consumer waited for a free reduction slot   */
+#define FNX_DEVERR_DRAIN 5         /* in-flight copies did not land before exit     */
+#define FNX_DEVERR_WAIT_X 6        /* the activation rows did not arrive            */
+#define FNX_DEVERR_WAIT_PEER 7     /* another rank did not publish its greedy key   */
+#define FNX_DEVERR_PEER_DESYNC 8   /* another rank is two or more calls ahead       */
+#define FNX_DEVERR_ROUTES 9        /* a routing table the kernel cannot hold        */
+#define FNX_DEVERR_WAIT_EXPERT 10  /* a down projection waited for its expert's act */
+
 /* Split-K and argmax scratch of the dense GEMVs.  Counters and keys must be zero when
  * first used; every launch leaves them zero again (self-resetting, graph-replay safe).
  * Two launches that share one workspace must not run concurrently (the reference's
@@ -238,6 +253,11 @@ int fnx_ipc_get_handle(void* buf, void* handle);
 int fnx_ipc_open(const void* handle, void** buf);
 int fnx_ipc_close(void* buf);
 int fnx_peer_setup(void* local, void* const* bufs, int world, int rank);
+/* Limit of the in-kernel wait for the other ranks' keys, in nanoseconds (0 = the 2 s
+ * default); set after fnx_peer_setup, between calls.  An expired wait records
+ * FNX_DEVERR_WAIT_PEER and the rank keeps its own shard's token; a rank that finds
+ * another two or more calls ahead records FNX_DEVERR_PEER_DESYNC and does the same. */
+int fnx_peer_set_wait_limit(void* local, int64_t wait_ns);
 int fnx_w8a16_gemv_vocab_sharded(const void* x, int64_t ldx, const void* w, int64_t ldw,
                                  int w_dtype, const void* scale, int scale_kind, void* y,
                                  int64_t ldy, int out_f32, int64_t* argmax_out,
@@ -330,8 +350,9 @@ int fnx_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
  *   calls that may run at the same time (different streams without ordering) race on
  *   it.  The argmax keys, the argmax counter and the split-K counters must be zero when
  *   the kernel starts; each call clears them with a memset on its stream first.
- * - A device-side wait that gives up records its code in the array's error word,
- *   which this entry point does not report; fnx_w8a16_gemv with a workspace does.
+ * - A device-side wait that gives up records its code in the array's error word.  Each
+ *   call clears the word before its launch (with the keys and counters), so after the
+ *   call has finished fnx_static_ws_error reports whether that call's waits all ended.
  */
 #define FNX_STATIC_PARTIAL_FLOATS (256 * 1024)
 #define FNX_STATIC_COUNTERS 2048
@@ -342,6 +363,11 @@ int fnx_w8a16_gemv_static_ws(const void* x, int64_t ldx, const void* w, int64_t 
                              int64_t* argmax_out, unsigned long long* argmax_key_out,
                              int64_t row_offset, int M, int N, int K, const fnx_gemv_cfg* cfg,
                              int pdl, fnx_stream_t stream);
+/* The error word of fnx_w8a16_gemv_static_ws's array on the current device, read after
+ * the work on `stream` has finished (this call synchronises the stream); clear != 0 sets
+ * it back to zero.  *code receives an FNX_DEVERR_* value, or 0. */
+int fnx_static_ws_error(int clear, fnx_stream_t stream, int* code);
+
 /* Description of the last error of the calling thread ("" if none). */
 const char* fnx_last_error(void);
 

@@ -125,3 +125,49 @@ def test_two_rank_exchange_gloo():
         assert got == want
         assert want[1] == 17
         assert s == 3.0
+
+
+def test_reference_cfg_tuple_is_ignored():
+    """The reference's Triton 7-tuple cfg (w8a16_gemv.py:522-538) maps to the planner."""
+    assert w8._cfg((128, 64, 4, False, False, 4, 3)) is None
+    assert w8._cfg(None) is None
+    assert w8._cfg((8, 4)).warps == 8
+    with pytest.raises(ValueError):
+        w8._cfg((1, 2, 3, 4, 5, 6))
+
+
+def test_n_major_weight_is_declined():
+    """An N-contiguous [N, K] view (the reference's W_KN case) is declined with
+    NotImplementedError before any launch, so a caller keeps its own path."""
+    import flash_next_rtxpro6000_b200 as fx
+
+    N, K = 64, 128
+    x = torch.zeros(1, K, dtype=torch.bfloat16)
+    w = torch.zeros(K, N, dtype=torch.int8).t()  # [N, K], stride (1, N)
+    s = torch.ones(N)
+    with pytest.raises(NotImplementedError):
+        fx.w8a16_gemv(x, w, s)
+    with pytest.raises(NotImplementedError):
+        fx.w8a16_gemv_silu_mul(x, torch.zeros(K, 2 * N, dtype=torch.int8).t(), torch.ones(2 * N))
+
+
+def test_device_error_flags_are_read_and_cleared():
+    from flash_next_rtxpro6000_b200 import errors
+
+    f1 = torch.zeros(1, dtype=torch.int32)
+    f2 = torch.zeros(1, dtype=torch.int32)
+    errors.register(f1, "first")
+    errors.register(f2, "second")
+    errors.check_device_errors(torch.device("cpu"))  # nothing set
+    f2.fill_(7)
+    with pytest.raises(errors.DeviceWaitError) as ei:
+        errors.check_device_errors(torch.device("cpu"))
+    assert ei.value.codes == [("second", 7)]
+    assert "WAIT_PEER" in str(ei.value)
+    assert int(f2.item()) == 0  # cleared
+    errors.check_device_errors(torch.device("cpu"))
+    f1.fill_(9)
+    with pytest.raises(errors.DeviceWaitError):
+        errors.check_flag(f1, "first", clear=False)
+    assert int(f1.item()) == 9
+    f1.zero_()
