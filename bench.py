@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--ms", type=str, default=None, help="comma-separated token counts")
     ap.add_argument("--layers", type=int, default=48, help="MoE layers of --workload stack")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--moe-three", action="store_true",
+                    help="MoE: the three-launch layer instead of the fused one")
     ap.add_argument("--no-extra", action="store_true",
                     help="default workload: skip the MoE and NVFP4 GEMV lines")
     ap.add_argument("--no-e2e", action="store_true")
@@ -803,7 +805,8 @@ def bench_draft_step(args, fx, syn, dev):
 
 def bench_moe(args, fx, syn, dev, cpu=False):
     """Config 2 (NVFP4 MoE, 512 experts, top-10 + shared expert).  48 routings rotate over
-    shifted expert sets (> 4x L2 across the rotation) inside one CUDA graph."""
+    shifted expert sets (> 4x L2 across the rotation) inside one CUDA graph.  The layer
+    runs as one fused launch (``--moe-three`` times the three-launch form instead)."""
     import torch
 
     from flash_next_rtxpro6000_b200.w4a16_nvfp4_gemv import swizzle_blockscale
@@ -815,8 +818,9 @@ def bench_moe(args, fx, syn, dev, cpu=False):
     shared = fx.SharedExpert(L.sh_w13.to(dev), swizzle_blockscale(L.sh_s13.to(dev)),
                              L.sh_g13.to(dev), L.sh_w2.to(dev), swizzle_blockscale(L.sh_s2.to(dev)),
                              L.sh_g2.to(dev))
+    fused = not args.moe_three
     ws = fx.make_workspace(num_routes=10, hidden_size=syn.HIDDEN, intermediate_size=syn.INTER,
-                           device=dev)
+                           device=dev, fused=fused)
     results = {}
     peak, src = measured_peak()
     total_bytes, total_ms = 0, 0.0
@@ -858,8 +862,8 @@ def bench_moe(args, fx, syn, dev, cpu=False):
                            "bytes_per_call": int(bytes_per_call)}
         total_bytes += bytes_per_call * reps * n_rot
         total_ms += ms
-        launches += reps * n_rot * fx.moe_launches_per_call(M, syn.TOPK, syn.EXPERTS,
-                                                             syn.HIDDEN, syn.INTER)
+        launches += reps * n_rot * fx.moe_launches_per_call(syn.HIDDEN, syn.INTER, fused,
+                                                             num_tokens=M)
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9
     res = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
@@ -869,8 +873,9 @@ def bench_moe(args, fx, syn, dev, cpu=False):
            "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
                       "l2": f"{n_rot} routings over shifted expert sets in one CUDA graph (> 4x L2)"},
            "per_m": results,
-           "roofline": _roofline_per_m(results, peak, src, fx.moe_kernel_name(Ms[0]),
-                                       "moe_nvfp4_config2"),
+           "roofline": _roofline_per_m(results, peak, src,
+                                       fx.moe_kernel_name(syn.HIDDEN, syn.INTER, fused),
+                                       "moe_fused_config2" if fused else "moe_nvfp4_config2"),
            "clocks": clocks, "gpu_launches": launches}
     if cpu:
         cb = {}
@@ -973,7 +978,9 @@ def bench_stack(args, fx, syn, dev):
                          "argmax": am.cpu().tolist()}
         total_bytes += step_bytes * reps
         total_ms += ms
-        launches += reps * (3 * n_layers + 1)  # k1, k2, route sum per layer; lm_head
+        # MoE launches per layer (one fused, or gate/up + down + route sum); the lm_head
+        launches += reps * (fx.moe_launches_per_call(syn.HIDDEN, syn.INTER, num_tokens=M)
+                            * n_layers + 1)
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1,
@@ -1055,8 +1062,9 @@ def bench_moe_sharded(args, fx, syn, dev, rank, world):
                          "rank0_local_bytes_per_call": int(local_bytes / n_rot)}
         total_bytes += nbytes * reps
         total_ms += ms
-        launches += reps * n_rot * 3  # k1, k2, route sum (the NCCL sum and the bf16 copy
-        # are library kernels)
+        # the MoE kernels (the NCCL sum and the bf16 copy are library kernels)
+        launches += reps * n_rot * fx.moe_launches_per_call(syn.HIDDEN, syn.INTER, num_tokens=M,
+                                                             num_experts=E_local)
         torch.cuda.synchronize()
         del g
     value = total_bytes / (total_ms / 1e3) / 1e9

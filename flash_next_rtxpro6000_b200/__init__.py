@@ -45,9 +45,11 @@ from .draft_moe_gemv import (  # noqa: F401
     draft_moe_gemv,
     enable_draft_moe_gemv,
     make_workspace,
+    fused_tiling,
     moe_gemv,
     moe_kernel_name,
     moe_launches_per_call,
+    moe_plan,
     unsupported_reason,
 )
 

@@ -30,6 +30,7 @@ DEVICE_ERRORS = {
     8: "PEER_DESYNC: another rank is two or more calls ahead",
     9: "ROUTES: a routing table the kernel cannot hold",
     10: "WAIT_EXPERT: a down projection waited for its expert's activations",
+    11: "RING: a launch whose ring stages the waits cannot order",
 }
 
 EXPORTED = (
@@ -52,7 +53,10 @@ EXPORTED = (
     "fnx_peer_set_wait_limit",
     "fnx_w8a16_gemv_vocab_sharded",
     "fnx_w4a16_nvfp4_gemv",
+    "fnx_nvfp4_quantize",
+    "fnx_nvfp4_dequantize",
     "fnx_moe_workspace_bytes",
+    "fnx_plan_moe",
     "fnx_moe_gemv",
     "fnx_argmax_decode",
     "fnx_static_ws_error",
@@ -108,6 +112,8 @@ class FnxMoeWorkspace(ctypes.Structure):
         ("error_flag", c_void_p),
         ("max_m", c_int),
         ("max_routes", c_int),
+        ("counters", c_void_p),
+        ("n_counters", c_int64),
     ]
 
 
@@ -115,6 +121,7 @@ class FnxMoeWorkspaceSizes(ctypes.Structure):
     _fields_ = [
         ("act", c_int64),
         ("partials", c_int64),
+        ("counters", c_int64),
     ]
 
 
@@ -168,8 +175,14 @@ def _declare(lib):
         _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, c_int64, c_int64,
         c_int, _P, _P, c_int64, c_int, c_int, c_int, POINTER(FnxGemvCfg),
         POINTER(FnxWorkspace), c_int, _P]
+    lib.fnx_nvfp4_quantize.argtypes = [_P, c_int64, c_int, c_int, c_int, _P, c_int64, _P, c_int64,
+                                       _P, _P, _P]
+    lib.fnx_nvfp4_dequantize.argtypes = [_P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, c_int,
+                                         c_int, c_int, _P]
     lib.fnx_moe_workspace_bytes.argtypes = [c_int, c_int, c_int, c_int, c_int,
                                             POINTER(FnxMoeWorkspaceSizes)]
+    lib.fnx_plan_moe.argtypes = [c_int, c_int, c_int, c_int, c_int, POINTER(c_int), POINTER(c_int),
+                                 POINTER(c_int), POINTER(c_int64)]
     lib.fnx_moe_gemv.argtypes = [
         _P, c_int64, _P, _P, c_int, c_int, POINTER(FnxMoeWeights), POINTER(FnxMoeWeights), _P,
         c_int64, c_int, POINTER(FnxMoeWorkspace), c_int, _P]

@@ -914,6 +914,39 @@ int fnx_w4a16_nvfp4_gemv(const void* x, int64_t ldx, const void* wq, int64_t ldw
   return run_dense(c);
 }
 
+int fnx_nvfp4_quantize(const void* w, int64_t ldw, int w_f32, int N, int K, void* wq,
+                       int64_t ldwq, void* bs, int64_t ldbs, float* gscale,
+                       unsigned int* scratch, fnx_stream_t stream) {
+  g_err.clear();
+  if (N < 1 || K < 16 || K % 16) return fail(FNX_EINVAL, "N=%d, K=%d: K must be a multiple of 16", N, K);
+  if (!w || !wq || !bs || !gscale || !scratch) return fail(FNX_EINVAL, "null argument");
+  if (ldw < K || ldwq < K / 2 || ldbs < K / 16 || ldwq % 8 || !aligned(wq, 8))
+    return fail(FNX_EINVAL, "bad strides: need ldw >= K, ldwq >= K/2 (multiple of 8, wq 8-byte "
+                "aligned), ldbs >= K/16");
+  if (fnx::launch_nvfp4_quantize(w, ldw, w_f32, N, K, static_cast<uint8_t*>(wq), ldwq,
+                                 static_cast<uint8_t*>(bs), ldbs, gscale, scratch,
+                                 static_cast<cudaStream_t>(stream)))
+    return cuda_fail("NVFP4 quantise launch");
+  return FNX_OK;
+}
+
+int fnx_nvfp4_dequantize(const void* wq, int64_t ldwq, const void* bs, int64_t ldbs,
+                         const float* gscale, int gscale_per_row, void* out, int64_t ldo,
+                         int out_f32, int N, int K, fnx_stream_t stream) {
+  g_err.clear();
+  if (N < 0 || K < 16 || K % 16) return fail(FNX_EINVAL, "N=%d, K=%d: K must be a multiple of 16", N, K);
+  if (N == 0) return FNX_OK;
+  if (!wq || !bs || !gscale || !out) return fail(FNX_EINVAL, "null argument");
+  if (ldwq < K / 2 || ldbs < K / 16 || ldo < K || ldwq % 8 || !aligned(wq, 8))
+    return fail(FNX_EINVAL, "bad strides: need ldwq >= K/2 (multiple of 8, wq 8-byte aligned), "
+                "ldbs >= K/16, ldo >= K");
+  if (fnx::launch_nvfp4_dequantize(static_cast<const uint8_t*>(wq), ldwq,
+                                   static_cast<const uint8_t*>(bs), ldbs, gscale, gscale_per_row,
+                                   out, ldo, out_f32, N, K, static_cast<cudaStream_t>(stream)))
+    return cuda_fail("NVFP4 dequantise launch");
+  return FNX_OK;
+}
+
 int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, int I,
                             fnx_moe_workspace_sizes* out) {
   g_err.clear();
@@ -923,8 +956,48 @@ int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, i
   if (int rc = moe_geometry(max_m, max_routes, num_experts, H, I, geo)) return rc;
   const int64_t pairs = (int64_t)max_m * (max_routes + 1);
   const int64_t dcap = std::min<int64_t>(num_experts, (int64_t)max_m * max_routes) + 1;
-  out->act = dcap * 16 * (2LL * I + 64);
+  const int64_t vcap = fnx::fused_vcap(max_m, max_routes, num_experts);
+  // the three-launch form: 16 slots per distinct expert; the fused form: 8 per virtual one
+  out->act = std::max(dcap * 16, vcap * fnx::kFusedSlots) * (2LL * I + 64);
   out->partials = pairs * H * 4;
+  out->counters = vcap + H / 64 + 1;
+  return FNX_OK;
+}
+
+namespace {
+
+// Launch geometry of the fused layer: the deepest weight ring that fits beside the staged
+// activations, the act and result slots and the routing tables (at least 4 stages).
+int fused_plan(int M, int R, int E, int H, int I, int vcap, int& NG, int& NS, size_t& smem) {
+  const fnx::FusedLayout L0 = fnx::fused_layout(M, R, E, H, I, 0, vcap);
+  int64_t ns = ((int64_t)kMaxSmem - L0.total - 256) / (L0.stage_bytes + 16);
+  ns = std::min<int64_t>(ns, 12);
+  ns -= ns % fnx::kFusedRing;  // every stage owned by one producer warp and one consumer group
+  if (ns < 4)
+    return fail(FNX_EUNSUPPORTED, "fused MoE: shared memory too small for M=%d, H=%d, I=%d", M, H, I);
+  NG = fnx::kFusedMaxGroups;
+  NS = (int)ns;
+  smem = fnx::fused_layout(M, R, E, H, I, NS, vcap).total;
+  return FNX_OK;
+}
+
+}  // namespace
+
+int fnx_plan_moe(int M, int R, int E, int H, int I, int* fused, int* stages, int* groups,
+                 int64_t* smem_bytes) {
+  g_err.clear();
+  if (!fused) return fail(FNX_EINVAL, "null fused");
+  if (M < 1 || M > FNX_MAX_M || R < 1 || R > 32 || E < 1 || E > 4096)
+    return fail(FNX_EINVAL, "M=%d, R=%d, E=%d out of range", M, R, E);
+  int ng = 0, ns = 0;
+  size_t smem = 0;
+  const bool f = fnx::moe_fused_has(H, I) &&
+                 fused_plan(M, R, E, H, I, fnx::fused_vcap(M, R, E), ng, ns, smem) == FNX_OK;
+  g_err.clear();
+  *fused = f ? 1 : 0;
+  if (stages) *stages = f ? ns : 0;
+  if (groups) *groups = f ? ng : 0;
+  if (smem_bytes) *smem_bytes = f ? (int64_t)smem : 0;
   return FNX_OK;
 }
 
@@ -961,8 +1034,15 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   if (!ws->act || !ws->partials || ws->max_m < M || ws->max_routes < R)
     return fail(FNX_EINVAL, "MoE workspace missing or sized for fewer tokens/routes");
   if (!aligned(ws->act, 16)) return fail(FNX_EINVAL, "MoE workspace act rows must be 16-byte aligned");
-  // The routes of one token address act rows t * (R + 1) + r of the workspace's
-  // (max_routes + 1)-wide layout only when R == max_routes; use the call's R instead.
+  // the one-launch layer when the workspace has its counters, the tiling is compiled and
+  // its shared memory fits; otherwise the three-launch layer
+  int fng = 0, fns = 0;
+  size_t fsmem = 0;
+  const bool fused = ws->counters && fnx::moe_fused_has(H, I) &&
+                     fused_plan(M, R, E, H, I, fnx::fused_vcap(M, R, E), fng, fns, fsmem) == FNX_OK;
+  g_err.clear();
+  if (fused && (int64_t)ws->n_counters < (int64_t)fnx::fused_vcap(M, R, E) + H / 64 + 1)
+    return fail(FNX_EINVAL, "MoE workspace counters too few for M=%d, R=%d, E=%d", M, R, E);
   const int NT = M > 8 ? 2 : 1;
   const int sms = fnx::num_sms();
   const int has_shared = shared ? 1 : 0;
@@ -1005,6 +1085,22 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   a.out_f32 = out_f32;
   a.NT = NT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (fused) {
+    a.vcap = fnx::fused_vcap(M, R, E);
+    a.cnt = ws->counters;
+    a.NG = fng;
+    a.NS = fns;
+    const size_t smem = fsmem;
+    a.pdl = pdl;
+    // one CTA per SM at most (the CTAs wait for one another), never more than the items
+    const int64_t max_items = (int64_t)a.vcap * (I / 8 + H / 64);
+    const int grid = (int)std::min<int64_t>(max_items, sms);
+    const int rc = fnx::launch_moe_fused(a, grid, smem, st);
+    if (rc == 1) return fail(FNX_EUNSUPPORTED, "no fused MoE instance for H=%d, I=%d", H, I);
+    if (rc) return cuda_fail("fused MoE launch");
+    return FNX_OK;
+  }
 
   MoeGeo geo;
   if (int rc = moe_geometry(M, R, E, H, I, geo)) return rc;

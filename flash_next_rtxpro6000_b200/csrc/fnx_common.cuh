@@ -572,7 +572,8 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 // Device error codes (C ABI values, FNX_DEVERR_* in include/fnx_gemv.h).
 enum ErrCode : int { ERR_NONE = 0, ERR_WAIT_FULL = 1, ERR_WAIT_EMPTY = 2, ERR_WAIT_RED = 3,
                      ERR_WAIT_RFREE = 4, ERR_DRAIN = 5, ERR_WAIT_X = 6, ERR_WAIT_PEER = 7,
-                     ERR_PEER_DESYNC = 8, ERR_ROUTES = 9, ERR_WAIT_EXPERT = 10 };
+                     ERR_PEER_DESYNC = 8, ERR_ROUTES = 9, ERR_WAIT_EXPERT = 10,
+                     ERR_RING = 11 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);

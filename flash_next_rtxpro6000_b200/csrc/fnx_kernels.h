@@ -269,6 +269,10 @@ struct MoeArgs {
   // launch geometry (EW: k1 epilogue warps)
   int W, CPW, NS, RS, NT, EW;
   int pdl;
+  // fused single-launch form (moe_fused.cu): counters [vcap + H / 64 + 1] (zero between
+  // calls, left at zero), the virtual-expert capacity and the consumer groups
+  unsigned* cnt;
+  int vcap, NG;
 };
 
 // Shared-memory layout of the MoE kernels.  A stage holds the unit's weight tiles, its
@@ -347,6 +351,129 @@ __host__ __device__ inline MoeLayout moe_layout(int kernel /*1 = up, 2 = down*/,
   return L;
 }
 
+// ------------------------------------------------------------------------------------
+// Fused MoE layer (moe_fused.cu): one persistent launch, one CTA per SM.
+// ------------------------------------------------------------------------------------
+constexpr int kFusedSlots = 8;     // route slots of one virtual expert (MMA N = 8)
+constexpr int kFusedProd = 2;      // producer warps (items round robin; a bulk copy takes
+                                   // ~70 cycles to issue, warps issue in parallel)
+constexpr int kFusedFetch = 2;     // act fetcher warps
+constexpr int kFusedEpi = 8;       // epilogue warps (each release of stores costs its warp
+                                   // ~0.5-1 us, so several run side by side)
+constexpr int kFusedRes = 8;       // result slots (consumers -> epilogue warps)
+constexpr int kFusedBatch = 1;     // items whose stores one epilogue release covers
+constexpr int kFusedAct = 2;       // act ring slots (fetchers -> consumers)
+constexpr int kFusedMaxGroups = 2; // consumer groups of 4 warps
+constexpr int kFusedThreads = (kFusedProd + kFusedFetch + kFusedEpi + 4 * kFusedMaxGroups) * 32;
+// The rings use parity waits, which are only correct when one warp (producer side) and
+// one consumer group (consumer side) see every use of a slot in order, so that a slot's
+// barrier is never more than one phase behind the waiter.  Items go round robin to the
+// producer warps and to the consumer groups, so the stage count must be a multiple of
+// both: kFusedRing.  (Stage counts that broke this let a wait pass a phase early: a stage
+// was refilled while it was being read, and the exit drain could miss a copy in flight.)
+constexpr int kFusedRing = kFusedProd * kFusedMaxGroups /
+                           (kFusedProd % kFusedMaxGroups == 0   ? kFusedMaxGroups
+                            : kFusedMaxGroups % kFusedProd == 0 ? kFusedProd
+                                                                : 1);
+static_assert(kFusedRing % kFusedProd == 0 && kFusedRing % kFusedMaxGroups == 0,
+              "kFusedRing must be a common multiple of producers and consumer groups");
+static_assert(kFusedRes % kFusedEpi == 0 && kFusedRes % kFusedMaxGroups == 0,
+              "each result slot must belong to one epilogue warp and one consumer group");
+static_assert(kFusedAct % kFusedFetch == 0 && kFusedAct % kFusedMaxGroups == 0,
+              "each act slot must belong to one fetcher warp and one consumer group");
+
+// Capacity of the virtual-expert table for n = M * R routes over E experts: every
+// virtual expert holds 1..8 routes of one expert, so there are at most
+// min(E, n) + n / 8 of them, and never more than n; plus two shared-expert halves.
+__host__ __device__ inline int fused_vcap(int M, int R, int E) {
+  const int n = M * R;
+  const int d = E < n ? E : n;
+  const int v = d + n / 8;
+  return (v < n ? v : n) + 2;
+}
+
+// Shared-memory layout of the fused kernel (identical on host and device).  A ring stage
+// holds one work item: a gate/up tile (16 weight rows over H: the up and gate rows of 8
+// columns of I; their block scales; the expert's global scale) or a down half-block
+// (64 weight rows over I as four 16-row tiles; the 128-row block's scales).  An act slot
+// holds the 8 route rows of one virtual expert as scaled fp16, each followed by its
+// factor; a result slot holds the four consumer warps' C fragments of one item.
+struct FusedLayout {
+  int ub1, tb1, soff1, foff1;   // gate/up tile: row bytes, tile bytes, scale / scalar offsets
+  int ub2, tb2, soff2;          // down half-block
+  int stage_bytes, act_bytes, res_bytes;
+  int bars, stages, xs, act, res, unscale;
+  int lid, bitmap, wbase, exp_of, cnt_of, vbase, ctab, rrank, rdist, etok, vexp, vnum, vent,
+      misc, lastk, total;
+};
+
+__host__ __device__ inline FusedLayout fused_layout(int M, int R, int E, int H, int I, int NS,
+                                                    int vcap) {
+  FusedLayout L;
+  L.ub1 = H / 2;
+  L.tb1 = tile_bytes(L.ub1);
+  L.soff1 = L.tb1;
+  const int sc1 = 16 * dense_align(H / 16, 16);  // >= the swizzled 2 x 2 x (H / 64) x 16 B
+  L.foff1 = L.soff1 + sc1;
+  L.ub2 = I / 2;
+  L.tb2 = tile_bytes(L.ub2);
+  L.soff2 = 4 * L.tb2;
+  const int sc2 = 128 * (I / 16);                // the whole 128-row block (swizzled)
+  const int e1 = L.foff1 + 16, e2 = L.soff2 + sc2;
+  L.stage_bytes = dense_align(e1 > e2 ? e1 : e2, 128);
+  L.act_bytes = kFusedSlots * stage_row_bytes(I);  // factor of row s at s * row + 2I
+  L.res_bytes = 4 * 32 * 16 + 16;                  // + the expert's global scale (tiles)
+  const int n = M * R;
+  const int nw = (E + 31) / 32;
+  const int dcap = E < n ? E : n;
+  const int nchunk = (n + 31) / 32;
+  int off = 0;
+  L.bars = off;  // full, empty [NS]; xbar; afull, aempty [kFusedAct]; rfull, rfree [kFusedRes]
+  off = dense_align(off + (2 * NS + 1 + 2 * kFusedAct + 2 * kFusedRes) * 8, 128);
+  L.stages = off;
+  off += NS * L.stage_bytes;
+  L.xs = off;
+  off += M * stage_row_bytes(H);
+  L.act = dense_align(off, 128);
+  off = L.act + kFusedAct * L.act_bytes;
+  L.res = dense_align(off, 16);
+  off = L.res + kFusedRes * L.res_bytes;
+  L.unscale = dense_align(off, 16);
+  off = L.unscale + 32 * 4;
+  L.lid = off;
+  off += dense_align(2 * n, 16);
+  L.bitmap = off;
+  off += dense_align(4 * nw, 16);
+  L.wbase = off;
+  off += dense_align(4 * nw, 16);
+  L.exp_of = off;
+  off += dense_align(2 * dcap, 16);
+  L.cnt_of = off;
+  off += dense_align(2 * dcap, 16);
+  L.vbase = off;
+  off += dense_align(2 * dcap, 16);
+  L.ctab = off;
+  off += dense_align(nchunk * dcap, 16);
+  L.rrank = off;
+  off += dense_align(n, 16);
+  L.rdist = off;
+  off += dense_align(2 * n, 16);
+  L.etok = off;
+  off += dense_align(n, 16);
+  L.vexp = off;
+  off += dense_align(2 * vcap, 16);
+  L.vnum = off;
+  off += dense_align(vcap, 16);
+  L.vent = off;
+  off += dense_align(2 * kFusedSlots * vcap, 16);
+  L.misc = off;
+  off += 16;
+  L.lastk = off;  // [NS] last item issued into each ring stage
+  off += dense_align(4 * NS, 16);
+  L.total = dense_align(off, 128);
+  return L;
+}
+
 // MoE router: x . W^T (+ bias) into fp32 logits, then (topk > 0) the softmax top-k of
 // every row, run by the CTA that finishes last (router.cu).
 struct RouterArgs {
@@ -407,8 +534,19 @@ int launch_dense(const DenseArgs& a, int wtype, int nt, int cpw, int grid, size_
 int launch_moe_up(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream);
 int launch_moe_down(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_t stream);
 int launch_moe_sum(const MoeArgs& a, cudaStream_t stream);
+// The fused layer for the (H, I) tilings it is compiled for: 1 = no instance.
+int launch_moe_fused(const MoeArgs& a, int grid, size_t smem, cudaStream_t stream);
+bool moe_fused_has(int H, int I);
 int launch_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
                          cudaStream_t stream);
+
+// NVFP4 load-time codec (nvfp4_codec.cu).  scratch: one u32 (cleared here).
+int launch_nvfp4_quantize(const void* w, int64_t ldw, int w_f32, int N, int K, uint8_t* wq,
+                          int64_t ldwq, uint8_t* bs, int64_t ldbs, float* gscale,
+                          unsigned* scratch, cudaStream_t stream);
+int launch_nvfp4_dequantize(const uint8_t* wq, int64_t ldwq, const uint8_t* bs, int64_t ldbs,
+                            const float* gscale, int per_row, void* out, int64_t ldo, int out_f32,
+                            int N, int K, cudaStream_t stream);
 
 int dense_occupancy(int wtype, int nt, int cpw, int mode, int threads, size_t smem);
 int moe_up_occupancy(int nt, int cpw, int threads, size_t smem);

@@ -161,9 +161,13 @@ __device__ void route_decode(const MoeArgs& a, const Routing& rt) {
     for (int k = 0; k < (i >> 5); ++k) slot += rt.ctab[k * dcap + d];
     if (slot < kSlotCap) rt.ent[d * kSlotCap + slot] = (short)i;
   }
+  const int cap = a.NT == 2 ? kSlotCap : kSlotCap / 2;  // B columns of one unit
   for (int d = tid; d < D; d += nthreads) {
     int cnt = 0;
     for (int k = 0; k < nchunk; ++k) cnt += rt.ctab[k * dcap + d];
+    // more routes on one expert than one unit's B columns: the surplus routes would be
+    // dropped; report it (the fused form splits such experts instead)
+    if (cnt > cap && blockIdx.x == 0) record_error(a.err, ERR_ROUTES);
     rt.cnt_of[d] = cnt < kSlotCap ? cnt : kSlotCap;
   }
   __syncthreads();

@@ -51,17 +51,18 @@ class DraftMoeWorkspace:
     """Scratch of one MoE layer call.  Every buffer is fully rewritten before it is read
     within a call, so nothing is cleared per call or graph replay."""
 
-    act: torch.Tensor              # uint8 rows of 2I + 64 B: bf16 act in the down kernel's
-                                   # B-operand order, row d * 16 + s = route slot s of
-                                   # distinct expert d
-    partials: torch.Tensor         # [P, H] fp32 route partials of the down kernel
+    act: torch.Tensor              # uint8 rows of 2I + 64 B: bf16 act in the down
+                                   # projection's B-operand order, one row per route slot
+    partials: torch.Tensor         # [P, H] fp32 route partials of the down projection
     error_flag: torch.Tensor       # [1] int32 device error code (0 = none)
     max_tokens: int
     num_routes: int
+    counters: Optional[torch.Tensor] = None  # int32, zero between calls: the one-launch form
 
     def to_c(self) -> FnxMoeWorkspace:
+        n = 0 if self.counters is None else self.counters.numel()
         return FnxMoeWorkspace(ptr(self.act), ptr(self.partials), ptr(self.error_flag),
-                               self.max_tokens, self.num_routes)
+                               self.max_tokens, self.num_routes, ptr(self.counters), n)
 
 
 @dataclass
@@ -107,8 +108,11 @@ def unsupported_reason(*, hidden_size: int, intermediate_size: int,
 def make_workspace(*, num_routes: int, hidden_size: int, intermediate_size: int,
                    device: torch.device, cfg: DraftMoeGemvConfig = DEFAULT_CONFIG,
                    max_tokens: Optional[int] = None,
-                   num_experts: int = 4096) -> DraftMoeWorkspace:
-    """Scratch of one MoE layer call (0112-...patch:307-325), sized for max_tokens."""
+                   num_experts: int = 4096, fused: bool = True) -> DraftMoeWorkspace:
+    """Scratch of one MoE layer call (0112-...patch:307-325), sized for max_tokens.
+
+    ``fused`` (default) adds the counters of the one-launch layer; without them the layer
+    runs as three launches (gate/up, down, route sum)."""
     m = cfg.max_tokens if max_tokens is None else max_tokens
     sz = FnxMoeWorkspaceSizes()
     check(_lib.lib().fnx_moe_workspace_bytes(m, num_routes, num_experts, hidden_size,
@@ -121,6 +125,7 @@ def make_workspace(*, num_routes: int, hidden_size: int, intermediate_size: int,
         partials=torch.empty((pairs, hidden_size), dtype=torch.float32, device=device),
         error_flag=torch.zeros(1, dtype=torch.int32, device=device),
         max_tokens=m, num_routes=num_routes,
+        counters=torch.zeros(sz.counters, dtype=torch.int32, device=device) if fused else None,
     )
     errors.register(ws.error_flag, f"MoE workspace ({m} tokens x {num_routes} routes) on {device}")
     return ws
@@ -210,14 +215,52 @@ def draft_moe_gemv(
 moe_gemv = draft_moe_gemv
 
 
-def moe_launches_per_call(M: int, num_routes: int, num_experts: int, hidden_size: int,
-                          intermediate_size: int) -> int:
-    """Kernel launches one draft_moe_gemv call makes for these shapes."""
-    return 3
+_FUSED_TILINGS = ((2048, 512), (2560, 640), (1024, 256), (2048, 1024))  # (H, I)
 
 
-def moe_kernel_name(M: int) -> str:
+def fused_tiling(hidden_size: int, intermediate_size: int) -> bool:
+    """Whether the one-launch layer is compiled for this (H, I)."""
+    return (hidden_size, intermediate_size) in _FUSED_TILINGS
+
+
+def moe_plan(num_tokens: int, top_k: int, num_experts: int, hidden_size: int,
+             intermediate_size: int) -> dict:
+    """The form a call with a fused workspace takes (``fnx_plan_moe``): ``fused`` and, for
+    the one-launch layer, its weight-ring ``stages``, consumer ``groups`` and dynamic
+    shared memory ``smem_bytes``."""
+    f, ns, ng = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    sm = ctypes.c_int64()
+    check(_lib.lib().fnx_plan_moe(num_tokens, top_k, num_experts, hidden_size, intermediate_size,
+                                  ctypes.byref(f), ctypes.byref(ns), ctypes.byref(ng),
+                                  ctypes.byref(sm)), "fnx_plan_moe")
+    return {"fused": bool(f.value), "stages": ns.value, "groups": ng.value,
+            "smem_bytes": sm.value}
+
+
+def _one_launch(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts) -> bool:
+    if not (fused and fused_tiling(hidden_size, intermediate_size)):
+        return False
+    if num_tokens is None:
+        return True
+    return moe_plan(num_tokens, top_k, num_experts, hidden_size, intermediate_size)["fused"]
+
+
+def moe_launches_per_call(hidden_size: int, intermediate_size: int, fused: bool = True,
+                          num_tokens: Optional[int] = None, top_k: int = 10,
+                          num_experts: int = 512) -> int:
+    """Kernel launches of one draft_moe_gemv call with a workspace made with ``fused``
+    (for ``num_tokens`` tokens when given: the one-launch layer needs its shared memory
+    to fit, else the call takes the three-launch form)."""
+    one = _one_launch(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts)
+    return 1 if one else 3
+
+
+def moe_kernel_name(hidden_size: int, intermediate_size: int, fused: bool = True,
+                    num_tokens: Optional[int] = None, top_k: int = 10,
+                    num_experts: int = 512) -> str:
     """The kernel(s) one draft_moe_gemv call runs."""
+    if _one_launch(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts):
+        return "moe_fused_kernel"
     return "moe_up_kernel + moe_down_kernel + moe_sum_kernel"
 
 

@@ -10,8 +10,8 @@ scalar or ``[N]``.  The kernel decodes e2m1 natively (``cvt.rn.f16x2.e2m1x2``), 
 2^14 factor appears anywhere.
 
 ``quantize_nvfp4`` / ``dequantize_nvfp4`` are the load-time codec (ModelOpt convention,
-w4a16_nvfp4_gemv.py:426-510), written here with torch tensor ops on the weight's device;
-they are not on the decode path.
+w4a16_nvfp4_gemv.py:426-510), run by the library's codec kernels on the GPU; they are not
+on the decode path.
 """
 
 from __future__ import annotations
@@ -34,11 +34,6 @@ from .w8a16_gemv import (
 )
 
 FP4_SCALE_BLOCK = 16
-E4M3_MAX = 448.0
-E2M1_MAX = 6.0
-_E2M1_LEVELS = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
-_E2M1_MID = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)
-_TIE_UP = (0.75, 1.75, 3.5)
 
 
 def w4a16_nvfp4_gemv(
@@ -78,65 +73,77 @@ def w4a16_nvfp4_gemv(
     return y if y2 is None else (y, y2)
 
 
-def _round_e2m1(a: torch.Tensor) -> torch.Tensor:
-    """|a| in block-scale units -> magnitude code 0..7, nearest level, ties to the even code."""
-    mids = torch.tensor(_E2M1_MID, dtype=torch.float32, device=a.device)
-    idx = torch.bucketize(a, mids, right=False)
-    tie = (a == _TIE_UP[0]) | (a == _TIE_UP[1]) | (a == _TIE_UP[2])
-    return (idx + tie).clamp_(0, 7).to(torch.uint8)
+_SCRATCH: dict = {}
 
 
-def quantize_nvfp4(w: torch.Tensor, block: int = FP4_SCALE_BLOCK, row_chunk: int = 4096):
-    """[N, K] weight -> (wq [N, K//2] uint8, bs [N, K//16] uint8 e4m3 bits, gscale fp32 [1]).
+def quantize_nvfp4(w: torch.Tensor, block: int = FP4_SCALE_BLOCK):
+    """[N, K] bf16 / fp32 CUDA weight -> (wq [N, K//2] uint8, bs [N, K//16] uint8 e4m3 bits,
+    gscale fp32 [1]), computed by the library's codec kernels on the weight's device.
 
-    gscale = amax(|W|) / (448 * 6); per 16-block scale amax_b / 6 * (1 / gscale) rounded
-    to e4m3; codes = round_e2m1(W / (e4m3(bs) / (1 / gscale))).  Chunked over rows so the
-    transient is row_chunk * K fp32.
+    The ModelOpt convention (w4a16_nvfp4_gemv.py:426-472): gscale = max|W| / (448 * 6);
+    each 16-block's scale amax_b / 6 / gscale rounded to e4m3; codes = W / (e4m3 scale *
+    gscale) rounded to e2m1 with ties to even.  The codes equal the reference's bit for bit.
     """
+    if block != FP4_SCALE_BLOCK:
+        raise NotImplementedError("NVFP4 blocks are 16 values")
+    if not w.is_cuda:
+        raise NotImplementedError("quantize_nvfp4 runs on the GPU; move the weight to CUDA first")
     assert w.dim() == 2 and w.shape[1] % block == 0
+    if w.dtype not in (torch.bfloat16, torch.float32):
+        w = w.float()
+    if w.stride(1) != 1:
+        w = w.contiguous()
     N, K = w.shape
-    gmax = torch.zeros((), dtype=torch.float32, device=w.device)
-    for r0 in range(0, N, row_chunk):
-        gmax = torch.maximum(gmax, w[r0:r0 + row_chunk].float().abs().amax())
-    gscale = (gmax / (E4M3_MAX * E2M1_MAX)).clamp_(min=1e-30)
-    enc = 1.0 / gscale
     wq = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
     bs = torch.empty((N, K // block), dtype=torch.uint8, device=w.device)
-    for r0 in range(0, N, row_chunk):
-        r1 = min(N, r0 + row_chunk)
-        blk = w[r0:r1].float().view(r1 - r0, K // block, block)
-        amax = blk.abs().amax(dim=-1)
-        sb8 = (amax / E2M1_MAX * enc).clamp_(min=0.0, max=E4M3_MAX).to(torch.float8_e4m3fn)
-        bs[r0:r1] = sb8.view(torch.uint8)
-        eff = (sb8.float() / enc).unsqueeze(-1)
-        a = torch.where(eff > 0, blk / eff.clamp(min=1e-38), torch.zeros_like(blk))
-        code = (_round_e2m1(a.abs()) | (a < 0).to(torch.uint8) * 8).reshape(r1 - r0, K)
-        wq[r0:r1] = code[:, 0::2] | (code[:, 1::2] << 4)
-    return wq, bs, gscale.reshape(1)
-
-
-_LEVELS: dict = {}
+    gscale = torch.empty(1, dtype=torch.float32, device=w.device)
+    scratch = _SCRATCH.get(w.device)
+    if scratch is None:
+        scratch = torch.zeros(1, dtype=torch.int32, device=w.device)
+        _SCRATCH[w.device] = scratch
+    with torch.cuda.device(w.device):
+        rc = _lib.lib().fnx_nvfp4_quantize(
+            ptr(w), w.stride(0), int(w.dtype == torch.float32), N, K, ptr(wq), wq.stride(0),
+            ptr(bs), bs.stride(0), ptr(gscale), ptr(scratch),
+            torch.cuda.current_stream(w.device).cuda_stream)
+    check(rc, "quantize_nvfp4")
+    return wq, bs, gscale
 
 
 def dequantize_nvfp4(wq: torch.Tensor, bs: torch.Tensor, gscale: torch.Tensor,
-                     block: int = FP4_SCALE_BLOCK) -> torch.Tensor:
-    """fp32 [N, K] weight (the wide-M fallback and the numerics reference).  The level
-    table is cached per device so the call is graph-capture safe."""
+                     block: int = FP4_SCALE_BLOCK, dtype: torch.dtype = torch.float32,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[N, K] weight (fp32 by default, or bf16) from CUDA NVFP4 tensors, by the library's
+    codec kernel: e2m1(code) * (e4m3(bs) * gscale), gscale scalar or [N]
+    (w4a16_nvfp4_gemv.py:489-510).  No host synchronisation (graph-capture safe)."""
+    if block != FP4_SCALE_BLOCK:
+        raise NotImplementedError("NVFP4 blocks are 16 values")
+    if not wq.is_cuda:
+        raise NotImplementedError("dequantize_nvfp4 runs on the GPU")
     N, KH = wq.shape
     K = KH * 2
-    lvl = _LEVELS.get(wq.device)
-    if lvl is None:
-        lvl = torch.tensor(_E2M1_LEVELS, dtype=torch.float32, device=wq.device)
-        _LEVELS[wq.device] = lvl
-    code = torch.empty((N, K), dtype=torch.uint8, device=wq.device)
-    code[:, 0::2] = wq & 0x0F
-    code[:, 1::2] = wq >> 4
-    mag = lvl[(code & 0x07).long()]
-    val = torch.where((code & 0x08) > 0, -mag, mag)
-    g = gscale.to(wq.device, torch.float32).reshape(-1)
-    g = g.reshape(-1, 1) if g.numel() > 1 else g.reshape(1, 1)
-    s = bs.view(torch.float8_e4m3fn).float() * g
-    return val * s.repeat_interleave(block, dim=1)
+    if dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("dtype must be float32 or bfloat16")
+    bs = bs.view(torch.uint8) if bs.dtype != torch.uint8 else bs
+    g = gscale.reshape(-1)
+    if g.dtype != torch.float32 or not g.is_contiguous():
+        g = g.float().contiguous()
+    if g.numel() not in (1, N):
+        raise ValueError(f"gscale must be a scalar or [{N}]")
+    if wq.stride(1) != 1 or wq.stride(0) % 8 or wq.data_ptr() % 8:
+        wq = wq.contiguous()
+    if bs.stride(1) != 1:
+        bs = bs.contiguous()
+    y = torch.empty((N, K), dtype=dtype, device=wq.device) if out is None else out
+    if tuple(y.shape) != (N, K) or y.dtype != dtype or y.stride(1) != 1:
+        raise ValueError(f"out must be a row-contiguous {dtype} [{N}, {K}] tensor")
+    with torch.cuda.device(wq.device):
+        rc = _lib.lib().fnx_nvfp4_dequantize(
+            ptr(wq), wq.stride(0), ptr(bs), bs.stride(0), ptr(g), int(g.numel() > 1), ptr(y),
+            y.stride(0), int(dtype == torch.float32), N, K,
+            torch.cuda.current_stream(wq.device).cuda_stream)
+    check(rc, "dequantize_nvfp4")
+    return y
 
 
 def swizzle_blockscale(scale: torch.Tensor) -> torch.Tensor:

@@ -31,6 +31,8 @@
  *                            of argmax keys it replaces has no counterpart in the reference,
  *                            which serves one GPU); fnx_peer_* / fnx_ipc_* set its buffers up
  *   fnx_w4a16_nvfp4_gemv     kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:342-401
+ *   fnx_nvfp4_quantize / fnx_nvfp4_dequantize  w4a16_nvfp4_gemv.py:426-510 (quantize_nvfp4,
+ *                            dequantize_nvfp4; the load-time codec)
  *   fnx_moe_gemv             patches/sglang/series/0112-DG1-one-token-draft-MoE-as-a-W4A16-
  *                            NVFP4-Triton-GEMV.patch:328-386 (draft_moe_gemv), generalised
  *                            from one token to M <= 16
@@ -87,6 +89,7 @@ typedef void* fnx_stream_t;
 #define FNX_DEVERR_PEER_DESYNC 8   /* another rank is two or more calls ahead       */
 #define FNX_DEVERR_ROUTES 9        /* a routing table the kernel cannot hold        */
 #define FNX_DEVERR_WAIT_EXPERT 10  /* a down projection waited for its expert's act */
+#define FNX_DEVERR_RING 11         /* a launch whose ring stages the waits cannot order */
 
 /* Split-K and argmax scratch of the dense GEMVs.  Counters and keys must be zero when
  * first used; every launch leaves them zero again (self-resetting, graph-replay safe).
@@ -281,6 +284,23 @@ int fnx_w4a16_nvfp4_gemv(const void* x, int64_t ldx, const void* wq, int64_t ldw
                          int N, int K, const fnx_gemv_cfg* cfg, const fnx_workspace* ws,
                          int pdl, fnx_stream_t stream);
 
+/*
+ * NVFP4 load-time codec on the GPU (quantize_nvfp4 / dequantize_nvfp4,
+ * kernels/sglang/srt/layers/quantization/w4a16_nvfp4_gemv.py:426-510).
+ * fnx_nvfp4_quantize: w [N, K] bf16 (w_f32 == 0) or fp32, row stride ldw elements ->
+ *   wq uint8 [N, K/2] (low nibble = even k), bs e4m3 bytes [N, K/16], gscale[0] =
+ *   max(amax|w| / 2688, 1e-30); the codes equal the reference's bit for bit.  scratch: one
+ *   u32 of device memory (cleared by the call).  K % 16 == 0.
+ * fnx_nvfp4_dequantize: -> out [N, K] fp32 (out_f32) or bf16, value = e2m1(code) *
+ *   (e4m3(bs) * gscale), gscale scalar or [N] (gscale_per_row).
+ */
+int fnx_nvfp4_quantize(const void* w, int64_t ldw, int w_f32, int N, int K, void* wq,
+                       int64_t ldwq, void* bs, int64_t ldbs, float* gscale,
+                       unsigned int* scratch, fnx_stream_t stream);
+int fnx_nvfp4_dequantize(const void* wq, int64_t ldwq, const void* bs, int64_t ldbs,
+                         const float* gscale, int gscale_per_row, void* out, int64_t ldo,
+                         int out_f32, int N, int K, fnx_stream_t stream);
+
 /* NVFP4 expert bank in the server layout (ModelOptNvFp4FusedMoEMethod after
  * process_weights_after_loading, 0112-...patch:68-76). */
 typedef struct fnx_moe_weights {
@@ -300,27 +320,44 @@ typedef struct fnx_moe_weights {
 } fnx_moe_weights;
 
 typedef struct fnx_moe_workspace {
-  void* act;                     /* [D * 16, 2I + 64] bytes, D = min(E, max_m *        */
-                                 /* max_routes) + 1: bf16 act rows of each distinct     */
-                                 /* expert's route slots, in the k2 B-operand order     */
+  void* act;                     /* bf16 act rows of the routes (bytes: sizes.act)      */
   float* partials;               /* fp32 [max_m * (max_routes + 1), H]                  */
   int* error_flag;               /* device error code, or NULL                          */
   int max_m;                     /* capacity the buffers were sized for                 */
   int max_routes;
+  unsigned int* counters;        /* sizes.counters u32, zero when first used (every call */
+                                 /* leaves them zero), or NULL: the three-launch form    */
+  int64_t n_counters;
 } fnx_moe_workspace;
 
-/* Byte sizes of the fnx_moe_workspace buffers for (max_m, max_routes, E, H, I); also
- * checks that the library tiles these shapes (FNX_EUNSUPPORTED otherwise). */
+/* Sizes of the fnx_moe_workspace buffers for (max_m, max_routes, E, H, I): act and
+ * partials in bytes, counters in u32 entries; also checks that the library tiles these
+ * shapes (FNX_EUNSUPPORTED otherwise).  num_experts is the largest expert count the
+ * workspace will serve. */
 typedef struct fnx_moe_workspace_sizes {
-  int64_t act, partials;
+  int64_t act, partials, counters;
 } fnx_moe_workspace_sizes;
 
 int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, int I,
                             fnx_moe_workspace_sizes* out);
 
+/* The form fnx_moe_gemv takes for (M, R, E, H, I) with a workspace that has counters:
+ * *fused = 1 for the one-launch layer, with its weight-ring stages, consumer groups and
+ * dynamic shared memory; *fused = 0 (and zeros) for the three-launch layer.  Exposed for
+ * tests and launch accounting. */
+int fnx_plan_moe(int M, int R, int E, int H, int I, int* fused, int* stages, int* groups,
+                 int64_t* smem_bytes);
+
 /*
  * out[t, :] = sum_r topk_weights[t, r] * expert(topk_ids[t, r])(x[t]) [+ shared(x[t])]
- * expert(x) = w2 @ (silu(gate(x)) * up(x)); act rounded to bf16 between the GEMVs.
+ * expert(x) = w2 @ (silu(gate(x)) * up(x)); act rounded to bf16 between the GEMVs; the
+ * route sum in route order, then the shared expert (deterministic, no float atomics).
+ * With ws->counters (and H, I among the fused tilings: 2048 x 512, 2560 x 640,
+ * 1024 x 256, 2048 x 1024) the layer runs as ONE launch whose CTAs all run at once, one
+ * per SM; otherwise as three launches (gate/up, down, route sum).  Any routing is
+ * served: repeated ids and any number of routes per expert (the fused form; the
+ * three-launch form holds at most 8 routes per expert at M <= 8, 16 above, and records
+ * FNX_DEVERR_ROUTES for more).
  * x: bf16 [M, H] (row stride ldx); topk_ids int32 [M, R] (ids < 0 skipped);
  * topk_weights fp32 [M, R]; shared: an always-on expert with weight 1.0 (num_experts 1),
  * or NULL.  out: bf16 [M, H] (row stride ldo), or the fp32 partial sum of this expert

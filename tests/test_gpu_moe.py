@@ -64,16 +64,19 @@ def _oracle(L, x, ids, wts, shared=True, act_round=True, **kw):
                     order="server", act_round=act_round, **kw)
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
-def test_config2_matches_oracle(M):
+def test_config2_matches_oracle(M, fused):
+    """Config 2 at full size (512 experts) at every M, one-launch and three-launch forms."""
     import flash_next_rtxpro6000_b200 as fx
     from flash_next_rtxpro6000_b200 import synthetic as syn
 
-    E = 512 if M in (1, 16) else 64
+    E = 512
     L, d = _layer(E)
     x = syn.activations(M, seed=5)
     ids, wts = syn.routing(M, E=E, seed=M)
-    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev(),
+                           fused=fused)
     y = _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws)
     torch.cuda.synchronize()
     got = to_np(y)
@@ -222,3 +225,77 @@ def test_slice_without_routes_writes_zeros(out_f32):
         out=out, out_f32=out_f32)
     torch.cuda.synchronize()
     assert int(torch.count_nonzero(out)) == 0
+
+
+@pytest.mark.parametrize("M", [1, 16])
+def test_reference_model_shape(M):
+    """The reference model's MoE shape, H = 2560 and I = 640
+    (bench/bench/moe_smallm/model_shapes.py:24-30), in both forms."""
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(64, H=2560, I=640, seed=1)
+    x = syn.activations(M, K=2560, seed=11)
+    ids, wts = syn.routing(M, E=64, seed=110 + M)
+    ref = _oracle(L, x, ids, wts)
+    for fused in (True, False):
+        ws = fx.make_workspace(num_routes=10, hidden_size=2560, intermediate_size=640,
+                               device=dev(), fused=fused)
+        y = _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws)
+        torch.cuda.synchronize()
+        assert rel_err(to_np(y), ref) <= REL_TOL, fused
+        assert int(ws.error_flag.item()) == 0
+
+
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_crowded_and_repeated_routes(M):
+    """Routings the reference's kernels accept but that overfill one MMA block: every
+    token on the same few experts (up to 160 routes on one expert) and ids repeated
+    within a row.  The one-launch form splits such experts and matches the oracle; the
+    three-launch form reports FNX_DEVERR_ROUTES instead of dropping routes silently."""
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import errors
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(64)
+    x = syn.activations(M, seed=12)
+    _, wts = syn.routing(M, E=64, seed=12)
+    g = torch.Generator().manual_seed(M)
+    cases = [torch.randint(0, 3, (M, 10), generator=g, dtype=torch.int32),  # 3 experts
+             torch.full((M, 10), 7, dtype=torch.int32)]                     # one expert
+    for ids in cases:
+        ref = _oracle(L, x, ids, wts)
+        ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512,
+                               device=dev())
+        y = _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws)
+        torch.cuda.synchronize()
+        assert rel_err(to_np(y), ref) <= REL_TOL
+        errors.check_flag(ws.error_flag, "fused MoE")  # no error
+        ws3 = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512,
+                                device=dev(), fused=False)
+        y3 = _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws3)
+        torch.cuda.synchronize()
+        crowd = int(torch.bincount(ids.reshape(-1).long()).max())
+        if crowd > (16 if M > 8 else 8):  # more routes on one expert than one unit holds
+            with pytest.raises(errors.DeviceWaitError) as ei:
+                errors.check_flag(ws3.error_flag, "three-launch MoE")
+            assert [c for _, c in ei.value.codes] == [9]
+        else:
+            errors.check_flag(ws3.error_flag, "three-launch MoE")
+            assert rel_err(to_np(y3), ref) <= REL_TOL
+
+
+def test_fused_counters_return_to_zero():
+    """The one-launch layer leaves its counters at zero (graph replays need no memset)."""
+    import flash_next_rtxpro6000_b200 as fx
+    from flash_next_rtxpro6000_b200 import synthetic as syn
+
+    L, d = _layer(512)
+    ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    for M in (1, 3, 16):
+        x = syn.activations(M, seed=13 + M)
+        ids, wts = syn.routing(M, E=512, seed=130 + M)
+        _run(fx, d, x.to(dev()), ids.to(dev()), wts.to(dev()), ws)
+        torch.cuda.synchronize()
+        assert int(torch.count_nonzero(ws.counters)) == 0
+        assert int(ws.error_flag.item()) == 0

@@ -149,3 +149,25 @@ def test_quantize_nvfp4_on_device_matches_oracle():
     assert np.array_equal(gs.cpu().numpy(), ogs)
     deq = fx.dequantize_nvfp4(wq, bs, gs)
     assert np.array_equal(deq.cpu().numpy(), onv.dequantize(owq, obs, ogs))
+
+
+@pytest.mark.parametrize("case", ["randn", "allcodes", "zero_blocks", "ties", "row_spread"])
+def test_quantize_kernel_matches_reference_golden(case):
+    """The GPU codec against the reference's own quantize_nvfp4 / dequantize_nvfp4 outputs
+    (tests/golden/nvfp4_codec.npz, made by tests/golden/make_golden.py): codes, block
+    scales and global scale bit for bit (ties, all-zero blocks, every code, rows spanning
+    five decades), dequantisation bit for bit, from bf16 and from fp32 input."""
+    import os
+
+    fx = _fx()
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "nvfp4_codec.npz"))
+    w = torch.from_numpy(g[f"{case}_w"])
+    for src in (w.bfloat16(), w):  # the golden inputs are bf16 values stored as fp32
+        wq, bs, gs = fx.quantize_nvfp4(src.to(dev()))
+        assert np.array_equal(wq.cpu().numpy(), g[f"{case}_wq"])
+        assert np.array_equal(bs.cpu().numpy(), g[f"{case}_bs"])
+        assert np.array_equal(gs.cpu().numpy().reshape(-1), g[f"{case}_gscale"].reshape(-1))
+        deq = fx.dequantize_nvfp4(wq, bs, gs)
+        assert np.array_equal(deq.cpu().numpy().view(np.uint32), g[f"{case}_deq"].view(np.uint32))
+        deq16 = fx.dequantize_nvfp4(wq, bs, gs, dtype=torch.bfloat16)
+        assert torch.equal(deq16.cpu(), torch.from_numpy(g[f"{case}_deq"]).bfloat16())

@@ -171,3 +171,32 @@ def test_device_error_flags_are_read_and_cleared():
         errors.check_flag(f1, "first", clear=False)
     assert int(f1.item()) == 9
     f1.zero_()
+
+
+@pytest.mark.parametrize("H,I", [(2048, 512), (2560, 640), (1024, 256), (2048, 1024)])
+def test_fused_moe_ring_stages_are_owned(H, I):
+    """The one-launch MoE layer hands ring stages round robin to its producer warps and
+    consumer groups and waits on them by phase parity, which is only sound when every
+    stage belongs to one producer warp and one consumer group: the stage count must be a
+    multiple of both (an odd count faulted on the GPU).  The planner guarantees it for
+    every token count, routing width and expert count; a form that does not fit falls back
+    to the three-launch layer, which the launch accounting follows."""
+    import flash_next_rtxpro6000_b200 as fx
+
+    seen = set()
+    for M in range(1, 17):
+        for R in (1, 8, 10, 32):
+            for E in (1, 64, 256, 512):
+                p = fx.moe_plan(M, R, E, H, I)
+                if not p["fused"]:
+                    assert p["stages"] == 0
+                    assert fx.moe_launches_per_call(H, I, num_tokens=M, top_k=R, num_experts=E) == 3
+                    continue
+                ns, ng = p["stages"], p["groups"]
+                assert ng >= 1 and ns >= 4
+                assert ns % ng == 0 and ns % 2 == 0, (M, R, E, ns, ng)
+                assert 0 < p["smem_bytes"] <= 227 * 1024
+                assert fx.moe_launches_per_call(H, I, num_tokens=M, top_k=R, num_experts=E) == 1
+                seen.add(ns)
+    if (H, I) != (2048, 1024):
+        assert seen, "the fused layer is planned for some shape"
