@@ -23,8 +23,10 @@ the hand-written CUDA library ``_fnx.so``):
 from .w8a16_gemv import (  # noqa: F401
     GemvConfig,
     bf16_gemv,
+    dense_path,
     prealloc,
     scratch_slot,
+    set_dense_path,
     w8a16_gemv,
     w8a16_gemv_norm_gated,
     w8a16_gemv_norm_gated_supported,

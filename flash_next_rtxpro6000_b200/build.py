@@ -23,7 +23,8 @@ INCLUDE = PKG.parent / "include"
 LIB_PATH = PKG / "_fnx.so"
 OBJ_DIR = PKG / "_build"
 
-SOURCES = ["fnx_api.cu", "dense_gemv.cu", "dense_gemv_slice.cu", "dense_gemv_norm.cu", "moe_gemv.cu",
+SOURCES = ["fnx_api.cu", "dense_gemv.cu", "dense_gemv_slice.cu", "dense_gemv_norm.cu", "dense_tc.cu",
+           "moe_gemv.cu",
            "moe_fused.cu", "nvfp4_codec.cu", "router.cu", "topk1.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",

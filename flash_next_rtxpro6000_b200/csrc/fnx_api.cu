@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstddef>
 #include <cstring>
 #include <cstdarg>
@@ -81,6 +82,12 @@ int chunk_k(int wt) {
 }
 
 constexpr size_t kMaxSmem = 227 * 1024;
+
+// Dense GEMV form (fnx_set_dense_path): by default the tensor-core form serves M > kTcMinM.
+// Measured on the int8 lm_head (151,936 x 2,048) on B200: M = 9 / 16 tcgen05 70.2 / 74.0 us
+// against mma.sync 77.6 / 79.7 us; M = 1 / 8 mma.sync 51.8 / 57.0 us against 66.3 / 69.7.
+std::atomic<int> g_dense_path{FNX_DENSE_PATH_AUTO};
+constexpr int kTcMinM = 8;
 
 // Geometry of one dense call.  A work unit is RT 16-row tiles x (K / ksplit); each of
 // the W consumer warps streams CPW 64-byte chunks of every row of one tile; the weight
@@ -305,14 +312,66 @@ int run_dense(const DenseCall& c) {
   if (c.row_offset < 0 || c.row_offset + c.N > 0xFFFFFFFFLL)
     return fail(FNX_EINVAL, "row ids must fit in 32 bits");
 
+  const bool chain_on = c.chain.topk_index || c.chain.topk_p || c.chain.draft_tokens ||
+                        c.chain.positions;
+  const bool want_argmax = c.argmax_out || c.argmax_key_out || chain_on || c.peerbuf;
+  if (want_argmax && (!c.ws || !c.ws->argmax_keys || !c.ws->argmax_count))
+    return fail(FNX_EINVAL, "argmax needs the workspace's argmax_keys/argmax_count");
+
+  // The tensor-core form (tcgen05, A dequantised into tensor memory) at the verify widths:
+  // int8 / fp8 weights, no fused SiLU / norm / draft chain, the planner's own tiling, and
+  // a workspace for the partial sums of the blocks that CTAs share.
+  const int path = g_dense_path.load(std::memory_order_relaxed);
+  if (path != FNX_DENSE_PATH_MMA && !c.cfg && !c.silu && c.norm.G == 0 && !chain_on &&
+      (c.wt == FNX_W_INT8 || c.wt == FNX_W_FP8_E4M3) &&
+      (path == FNX_DENSE_PATH_TCGEN05 || c.M > kTcMinM)) {
+    int ns = 0;
+    size_t smem = 0;
+    const int grid = fnx::dense_tc_grid(c.N, c.K);
+    if (fnx::dense_tc_plan(c.wt, c.K, ns, smem) && c.ws && c.ws->partials && c.ws->counters &&
+        c.ws->partial_floats >= fnx::dense_tc_partial_floats(grid) &&
+        c.ws->n_counters >= fnx::dense_tc_counters(grid)) {
+      fnx::DenseArgs a = {};
+      a.x = c.x;
+      a.ldx = c.ldx;
+      a.w = static_cast<const uint8_t*>(c.w);
+      a.ldw = c.ldw;
+      a.scale = c.scale;
+      a.scale_kind = c.scale_kind;
+      a.y = c.y;
+      a.ldy = c.ldy;
+      a.y2 = c.y2;
+      a.ldy2 = c.ldy2;
+      a.split_n = c.y2 ? c.split_n : 0;
+      a.out_f32 = c.out_f32;
+      a.am_keys = want_argmax ? c.ws->argmax_keys : nullptr;
+      a.am_count = want_argmax ? c.ws->argmax_count : nullptr;
+      a.am_out = c.argmax_out;
+      a.am_key_out = c.argmax_key_out;
+      a.row_offset = c.row_offset;
+      a.err = c.ws->error_flag;
+      a.M = c.M;
+      a.N = c.N;
+      a.K = c.K;
+      a.NS = ns;
+      a.pdl = c.pdl;
+      a.peerbuf = c.peerbuf;
+      const int rc = fnx::launch_dense_tc(a, c.wt, grid, smem, c.ws->partials, c.ws->counters,
+                                          c.stream);
+      if (rc == 0) return FNX_OK;
+      if (rc == 2) return cuda_fail("tensor-core GEMV launch");
+      if (path == FNX_DENSE_PATH_TCGEN05 && rc == 3)
+        return fail(FNX_EUNSUPPORTED, "tensor map of the weights could not be encoded");
+      // otherwise (no tensor-map encoder, no instance) the mma.sync form below
+    } else if (path == FNX_DENSE_PATH_TCGEN05 && !fnx::dense_tc_plan(c.wt, c.K, ns, smem)) {
+      return fail(FNX_EUNSUPPORTED, "tensor-core GEMV: K=%d does not fit", c.K);
+    }
+  }
+
   DensePlan p;
   int rc = plan_dense(c.M, c.N, c.K, c.wt, c.silu, c.cfg, p);
   if (rc) return rc;
   const int NT = c.M > 8 ? 2 : 1;
-
-  const bool chain_on = c.chain.topk_index || c.chain.topk_p || c.chain.draft_tokens ||
-                        c.chain.positions;
-  const bool want_argmax = c.argmax_out || c.argmax_key_out || chain_on || c.peerbuf;
   if (p.ksplit > 1) {
     const int64_t need = (int64_t)p.tile_groups * p.ksplit * p.RT * 256;
     if (!c.ws || !c.ws->partials || !c.ws->counters)
@@ -321,9 +380,6 @@ int run_dense(const DenseCall& c) {
       return fail(FNX_EINVAL, "workspace too small: need %lld floats and %d counters",
                   (long long)need, p.tile_groups);
   }
-  if (want_argmax && (!c.ws || !c.ws->argmax_keys || !c.ws->argmax_count))
-    return fail(FNX_EINVAL, "argmax needs the workspace's argmax_keys/argmax_count");
-
   // xslice (each CTA stages only its k split) needs a grid that is a multiple of ksplit
   // and, with the fused norm, a unit k extent that holds whole norm groups; otherwise
   // the full rows are staged (same tiling and workspace, larger shared memory).
@@ -484,6 +540,15 @@ int static_scratch(void** out) {
 }  // namespace
 
 extern "C" {
+
+int fnx_set_dense_path(int path, int* previous) {
+  g_err.clear();
+  if (path != FNX_DENSE_PATH_AUTO && path != FNX_DENSE_PATH_MMA && path != FNX_DENSE_PATH_TCGEN05)
+    return fail(FNX_EINVAL, "dense path %d must be FNX_DENSE_PATH_AUTO, _MMA or _TCGEN05", path);
+  const int prev = g_dense_path.exchange(path);
+  if (previous) *previous = prev;
+  return FNX_OK;
+}
 
 int fnx_plan_gemv(int M, int N, int K, int w_dtype, int fused_silu, int argmax,
                   fnx_gemv_cfg* out) {

@@ -552,6 +552,17 @@ int dense_occupancy(int wtype, int nt, int cpw, int mode, int threads, size_t sm
 int moe_up_occupancy(int nt, int cpw, int threads, size_t smem);
 int moe_down_occupancy(int nt, int cpw, int threads, size_t smem);
 
+// Tensor-core (tcgen05) dense GEMV (dense_tc.cu): int8 / fp8 weights, K a multiple of
+// 128, plain mode.  dense_tc_plan picks the ring depth and shared memory (false: not
+// available for this weight type / K); the launch needs dense_tc_partial_floats(grid)
+// partial floats and dense_tc_counters(grid) zeroed counters.
+bool dense_tc_plan(int wt, int K, int& NS, size_t& smem);
+int dense_tc_grid(int N, int K);
+int64_t dense_tc_partial_floats(int grid);
+int64_t dense_tc_counters(int grid);
+int launch_dense_tc(const DenseArgs& d, int wt, int grid, size_t smem, float* part, unsigned* pcnt,
+                    cudaStream_t stream);
+
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();
 // Raise a kernel's dynamic shared-memory limit once per device; false on failure.

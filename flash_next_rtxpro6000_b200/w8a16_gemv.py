@@ -431,6 +431,39 @@ def w8a16_gemv_norm_gated(
     return y
 
 
+_DENSE_PATHS = {"auto": 0, "mma": 1, "tcgen05": 2}
+
+
+def set_dense_path(path: str) -> str:
+    """Select the contraction of the dense GEMV calls made without ``cfg`` (process-wide):
+    ``"auto"`` (tcgen05 tensor cores for int8 / fp8 weights at M > 8, mma.sync otherwise),
+    ``"mma"`` or ``"tcgen05"`` (wherever it applies, at every M).  Returns the previous
+    setting."""
+    if path not in _DENSE_PATHS:
+        raise ValueError(f"dense path must be one of {sorted(_DENSE_PATHS)}, got {path!r}")
+    import ctypes
+
+    prev = ctypes.c_int(0)
+    check(_lib.lib().fnx_set_dense_path(_DENSE_PATHS[path], ctypes.byref(prev)), "set_dense_path")
+    return {v: k for k, v in _DENSE_PATHS.items()}[prev.value]
+
+
+class dense_path:
+    """Context manager running the calls inside it with ``set_dense_path(path)``."""
+
+    def __init__(self, path: str):
+        self.path = path
+        self.prev = "auto"
+
+    def __enter__(self):
+        self.prev = set_dense_path(self.path)
+        return self
+
+    def __exit__(self, *exc):
+        set_dense_path(self.prev)
+        return False
+
+
 def plan(M: int, N: int, K: int, w_dtype: torch.dtype, fused_silu: bool = False) -> GemvConfig:
     """The geometry the library's planner picks for a call."""
     c = FnxGemvCfg()

@@ -121,6 +121,22 @@ typedef struct fnx_gemv_cfg {
   int grid;
 } fnx_gemv_cfg;
 
+/* Which contraction the dense GEMV entry points use when cfg is NULL (process-wide):
+ *  FNX_DENSE_PATH_AUTO     tcgen05 tensor-core form (A dequantised into tensor memory,
+ *                          stream-K over 128-row blocks) for int8 / fp8 weights at M > 8,
+ *                          mma.sync elsewhere (the default);
+ *  FNX_DENSE_PATH_MMA      mma.sync form only;
+ *  FNX_DENSE_PATH_TCGEN05  tcgen05 form wherever it applies, at every M.
+ * The tcgen05 form needs K a multiple of 128 and a workspace of >= 4096 * SMs partial
+ * floats and >= 4 * SMs counters; it is skipped (mma.sync form) for the fused SiLU,
+ * gated-norm and draft-chain variants and when a cfg is given.  *previous (may be
+ * NULL) receives the earlier setting.  No counterpart in the reference (its GEMV is one
+ * Triton kernel). */
+#define FNX_DENSE_PATH_AUTO 0
+#define FNX_DENSE_PATH_MMA 1
+#define FNX_DENSE_PATH_TCGEN05 2
+int fnx_set_dense_path(int path, int* previous);
+
 /* Planner used when cfg is NULL (exposed for tests and workspace sizing). */
 int fnx_plan_gemv(int M, int N, int K, int w_dtype, int fused_silu, int argmax,
                   fnx_gemv_cfg* out);

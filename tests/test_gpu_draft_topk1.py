@@ -107,8 +107,10 @@ def test_fused_draft_head(M):
     assert torch.equal(dt[:, 4:5], ti) and torch.equal(p, torch.ones_like(p))
     assert torch.equal(pos, torch.arange(M, dtype=torch.int64, device=d) * 3 + 1)
     # same token as the plain GEMV's fused argmax, mapped
+    # (the fused draft step runs the mma.sync form at every M, so the plain call does too)
     am = torch.empty(M, dtype=torch.int64, device=d)
-    y = fx.w8a16_gemv(x, w, s, argmax_out=am)
+    with fx.dense_path("mma"):
+        y = fx.w8a16_gemv(x, w, s, argmax_out=am)
     assert torch.equal(y, logits) and torch.equal(hot[am].view(M, 1), ti)
     assert _ws_clear()
 

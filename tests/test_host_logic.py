@@ -200,3 +200,20 @@ def test_fused_moe_ring_stages_are_owned(H, I):
                 seen.add(ns)
     if (H, I) != (2048, 1024):
         assert seen, "the fused layer is planned for some shape"
+
+
+def test_dense_path_selector():
+    """fnx_set_dense_path switches the dense GEMV form process-wide and reports the
+    previous setting; an unknown name is a ValueError (the ABI's FNX_EINVAL)."""
+    import flash_next_rtxpro6000_b200 as fx
+
+    prev = fx.set_dense_path("mma")
+    try:
+        assert fx.set_dense_path("tcgen05") == "mma"
+        with fx.dense_path("mma"):
+            assert fx.set_dense_path("mma") == "mma"
+        assert fx.set_dense_path("auto") == "tcgen05"
+        with pytest.raises(ValueError):
+            fx.set_dense_path("wgmma")
+    finally:
+        fx.set_dense_path(prev)
