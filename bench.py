@@ -56,6 +56,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--moe-three", action="store_true",
                     help="MoE: the three-launch layer instead of the fused one")
+    ap.add_argument("--moe-path", choices=["auto", "fused"], default="auto",
+                    help="MoE one-launch layer: decode-width kernel for M = 1 (auto) or the "
+                         "general one at every M (fused)")
     ap.add_argument("--no-extra", action="store_true",
                     help="default workload: skip the MoE and NVFP4 GEMV lines")
     ap.add_argument("--no-e2e", action="store_true")
@@ -821,6 +824,17 @@ def bench_moe(args, fx, syn, dev, cpu=False):
     fused = not args.moe_three
     ws = fx.make_workspace(num_routes=10, hidden_size=syn.HIDDEN, intermediate_size=syn.INTER,
                            device=dev, fused=fused)
+    prev_path = fx.set_moe_path(getattr(args, "moe_path", "auto"))
+    try:
+        return _bench_moe_body(args, fx, syn, dev, cpu, L, d, shared, fused, ws)
+    finally:
+        fx.set_moe_path(prev_path)
+
+
+def _bench_moe_body(args, fx, syn, dev, cpu, L, d, shared, fused, ws):
+    import torch
+
+    Ms = [int(m) for m in (args.ms or "1,2,4,8,16").split(",")]
     results = {}
     peak, src = measured_peak()
     total_bytes, total_ms = 0, 0.0
@@ -873,8 +887,9 @@ def bench_moe(args, fx, syn, dev, cpu=False):
            "config": {"workload": "nvfp4_moe_512x2048x512_top10_shared", "M": Ms,
                       "l2": f"{n_rot} routings over shifted expert sets in one CUDA graph (> 4x L2)"},
            "per_m": results,
-           "roofline": _roofline_per_m(results, peak, src,
-                                       fx.moe_kernel_name(syn.HIDDEN, syn.INTER, fused),
+           "roofline": _roofline_per_m(results, peak, src, " | ".join(dict.fromkeys(
+                                           fx.moe_kernel_name(syn.HIDDEN, syn.INTER, fused,
+                                                              num_tokens=M) for M in Ms)),
                                        "moe_fused_config2" if fused else "moe_nvfp4_config2"),
            "clocks": clocks, "gpu_launches": launches}
     if cpu:

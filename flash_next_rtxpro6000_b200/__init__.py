@@ -51,7 +51,9 @@ from .draft_moe_gemv import (  # noqa: F401
     moe_gemv,
     moe_kernel_name,
     moe_launches_per_call,
+    moe_path,
     moe_plan,
+    set_moe_path,
     unsupported_reason,
 )
 

@@ -35,6 +35,7 @@ DEVICE_ERRORS = {
 
 EXPORTED = (
     "fnx_set_dense_path",
+    "fnx_set_moe_path",
     "fnx_plan_gemv",
     "fnx_gemv_workspace_need",
     "fnx_w8a16_gemv",
@@ -135,6 +136,7 @@ _I64P = POINTER(c_int64)
 
 def _declare(lib):
     lib.fnx_set_dense_path.argtypes = [c_int, POINTER(c_int)]
+    lib.fnx_set_moe_path.argtypes = [c_int, POINTER(c_int)]
     lib.fnx_plan_gemv.argtypes = [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(FnxGemvCfg)]
     lib.fnx_gemv_workspace_need.argtypes = [c_int, c_int, c_int, c_int, c_int,
                                             POINTER(FnxGemvCfg), _I64P, _I64P]

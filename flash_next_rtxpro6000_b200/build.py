@@ -25,7 +25,7 @@ OBJ_DIR = PKG / "_build"
 
 SOURCES = ["fnx_api.cu", "dense_gemv.cu", "dense_gemv_slice.cu", "dense_gemv_norm.cu", "dense_tc.cu",
            "moe_gemv.cu",
-           "moe_fused.cu", "nvfp4_codec.cu", "router.cu", "topk1.cu"]
+           "moe_fused.cu", "moe_lean.cu", "nvfp4_codec.cu", "router.cu", "topk1.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
          "-I" + str(INCLUDE)]

@@ -87,6 +87,8 @@ constexpr size_t kMaxSmem = 227 * 1024;
 // Measured on the int8 lm_head (151,936 x 2,048) on B200: M = 9 / 16 tcgen05 70.2 / 74.0 us
 // against mma.sync 77.6 / 79.7 us; M = 1 / 8 mma.sync 51.8 / 57.0 us against 66.3 / 69.7.
 std::atomic<int> g_dense_path{FNX_DENSE_PATH_AUTO};
+// MoE layer form (fnx_set_moe_path): by default the decode-width kernel serves M <= 8.
+std::atomic<int> g_moe_path{FNX_MOE_PATH_AUTO};
 constexpr int kTcMinM = 8;
 
 // Geometry of one dense call.  A work unit is RT 16-row tiles x (K / ksplit); each of
@@ -546,6 +548,15 @@ int fnx_set_dense_path(int path, int* previous) {
   if (path != FNX_DENSE_PATH_AUTO && path != FNX_DENSE_PATH_MMA && path != FNX_DENSE_PATH_TCGEN05)
     return fail(FNX_EINVAL, "dense path %d must be FNX_DENSE_PATH_AUTO, _MMA or _TCGEN05", path);
   const int prev = g_dense_path.exchange(path);
+  if (previous) *previous = prev;
+  return FNX_OK;
+}
+
+int fnx_set_moe_path(int path, int* previous) {
+  g_err.clear();
+  if (path != FNX_MOE_PATH_AUTO && path != FNX_MOE_PATH_FUSED)
+    return fail(FNX_EINVAL, "MoE path %d must be FNX_MOE_PATH_AUTO or _FUSED", path);
+  const int prev = g_moe_path.exchange(path);
   if (previous) *previous = prev;
   return FNX_OK;
 }
@@ -1056,6 +1067,14 @@ int fnx_plan_moe(int M, int R, int E, int H, int I, int* fused, int* stages, int
     return fail(FNX_EINVAL, "M=%d, R=%d, E=%d out of range", M, R, E);
   int ng = 0, ns = 0;
   size_t smem = 0;
+  if (g_moe_path.load(std::memory_order_relaxed) == FNX_MOE_PATH_AUTO &&
+      fnx::moe_lean_plan(M, R, E, H, I, fnx::num_sms(), ns, smem)) {
+    *fused = 2;
+    if (stages) *stages = ns;
+    if (groups) *groups = 2;
+    if (smem_bytes) *smem_bytes = (int64_t)smem;
+    return FNX_OK;
+  }
   const bool f = fnx::moe_fused_has(H, I) &&
                  fused_plan(M, R, E, H, I, fnx::fused_vcap(M, R, E), ng, ns, smem) == FNX_OK;
   g_err.clear();
@@ -1150,6 +1169,24 @@ int fnx_moe_gemv(const void* x, int64_t ldx, const int32_t* topk_ids,
   a.out_f32 = out_f32;
   a.NT = NT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // The decode-width layer (M <= 8, swizzled scales): every SM one CTA, all resident.
+  if (ws->counters && experts->scales_swizzled &&
+      g_moe_path.load(std::memory_order_relaxed) == FNX_MOE_PATH_AUTO &&
+      aligned(experts->w13_scale, 16) && aligned(experts->w2_scale, 16) &&
+      (!shared || (aligned(shared->w13_scale, 16) && aligned(shared->w2_scale, 16))) &&
+      (int64_t)ws->n_counters >= fnx::moe_lean_counters(M, R, E)) {
+    int lns = 0;
+    size_t lsmem = 0;
+    if (fnx::moe_lean_plan(M, R, E, H, I, sms, lns, lsmem)) {
+      a.cnt = ws->counters;
+      a.pdl = pdl;
+      const int rc = fnx::launch_moe_lean(a, lns, sms, lsmem, st);
+      if (rc == 0) return FNX_OK;
+      if (rc != 3) return cuda_fail("decode-width MoE launch");
+      // rc 3: the weights' tensor maps could not be encoded: the general layer below
+    }
+  }
 
   if (fused) {
     a.vcap = fnx::fused_vcap(M, R, E);

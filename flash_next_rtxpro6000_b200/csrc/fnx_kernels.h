@@ -536,6 +536,14 @@ int launch_moe_down(const MoeArgs& a, int nt, int grid, size_t smem, cudaStream_
 int launch_moe_sum(const MoeArgs& a, cudaStream_t stream);
 // The fused layer for the (H, I) tilings it is compiled for: 1 = no instance.
 int launch_moe_fused(const MoeArgs& a, int grid, size_t smem, cudaStream_t stream);
+// Decode-width MoE layer in one launch (moe_lean.cu): M = 1, swizzled scales, H and I
+// multiples of 256 (H <= 2048, I <= 512).  moe_lean_plan picks the ring depth and shared memory for a
+// grid of `grid` CTAs (all resident, one per SM); the launch needs moe_lean_counters(M, R,
+// E) zeroed counters in a.cnt and (min(E, M R) + 1) M I bf16 act values in a.act, and
+// returns 3 when the weights' tensor maps cannot be encoded.
+bool moe_lean_plan(int M, int R, int E, int H, int I, int grid, int& NS, size_t& smem);
+int64_t moe_lean_counters(int M, int R, int E);
+int launch_moe_lean(const MoeArgs& a, int NS, int grid, size_t smem, cudaStream_t stream);
 bool moe_fused_has(int H, int I);
 int launch_argmax_decode(const unsigned long long* keys, int64_t* out, int M,
                          cudaStream_t stream);

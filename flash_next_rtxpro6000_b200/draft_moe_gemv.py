@@ -223,26 +223,69 @@ def fused_tiling(hidden_size: int, intermediate_size: int) -> bool:
     return (hidden_size, intermediate_size) in _FUSED_TILINGS
 
 
+_MOE_PATHS = {"auto": 0, "fused": 1}
+
+
+def set_moe_path(path: str) -> str:
+    """Select the one-launch MoE layer (process-wide): ``"auto"`` (the decode-width
+    kernel for M = 1 with swizzled scales, the general one-launch kernel otherwise) or
+    ``"fused"`` (the general one-launch kernel at every M).  Returns the previous
+    setting."""
+    if path not in _MOE_PATHS:
+        raise ValueError(f"MoE path must be one of {sorted(_MOE_PATHS)}, got {path!r}")
+    prev = ctypes.c_int(0)
+    check(_lib.lib().fnx_set_moe_path(_MOE_PATHS[path], ctypes.byref(prev)), "set_moe_path")
+    return {v: k for k, v in _MOE_PATHS.items()}[prev.value]
+
+
+class moe_path:
+    """Context manager running the calls inside it with ``set_moe_path(path)``."""
+
+    def __init__(self, path: str):
+        self.path = path
+        self.prev = "auto"
+
+    def __enter__(self):
+        self.prev = set_moe_path(self.path)
+        return self
+
+    def __exit__(self, *exc):
+        set_moe_path(self.prev)
+        return False
+
+
+_FORMS = {0: "three", 1: "fused", 2: "lean"}
+
+
 def moe_plan(num_tokens: int, top_k: int, num_experts: int, hidden_size: int,
              intermediate_size: int) -> dict:
-    """The form a call with a fused workspace takes (``fnx_plan_moe``): ``fused`` and, for
-    the one-launch layer, its weight-ring ``stages``, consumer ``groups`` and dynamic
-    shared memory ``smem_bytes``."""
+    """The form a call with a fused workspace and swizzled scales takes
+    (``fnx_plan_moe``): ``form`` ("lean": the decode-width one-launch layer, "fused": the
+    general one-launch layer, "three": three launches), ``fused`` (one launch) and, for a
+    one-launch layer, its weight-ring ``stages``, consumer ``groups`` and dynamic shared
+    memory ``smem_bytes``."""
     f, ns, ng = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     sm = ctypes.c_int64()
     check(_lib.lib().fnx_plan_moe(num_tokens, top_k, num_experts, hidden_size, intermediate_size,
                                   ctypes.byref(f), ctypes.byref(ns), ctypes.byref(ng),
                                   ctypes.byref(sm)), "fnx_plan_moe")
-    return {"fused": bool(f.value), "stages": ns.value, "groups": ng.value,
-            "smem_bytes": sm.value}
+    return {"form": _FORMS[f.value], "fused": f.value > 0, "stages": ns.value,
+            "groups": ng.value, "smem_bytes": sm.value}
+
+
+def _form(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts) -> str:
+    if not fused:
+        return "three"
+    if num_tokens is None:
+        return "fused" if fused_tiling(hidden_size, intermediate_size) else "three"
+    form = moe_plan(num_tokens, top_k, num_experts, hidden_size, intermediate_size)["form"]
+    if form == "fused" and not fused_tiling(hidden_size, intermediate_size):
+        return "three"
+    return form
 
 
 def _one_launch(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts) -> bool:
-    if not (fused and fused_tiling(hidden_size, intermediate_size)):
-        return False
-    if num_tokens is None:
-        return True
-    return moe_plan(num_tokens, top_k, num_experts, hidden_size, intermediate_size)["fused"]
+    return _form(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts) != "three"
 
 
 def moe_launches_per_call(hidden_size: int, intermediate_size: int, fused: bool = True,
@@ -258,8 +301,11 @@ def moe_launches_per_call(hidden_size: int, intermediate_size: int, fused: bool 
 def moe_kernel_name(hidden_size: int, intermediate_size: int, fused: bool = True,
                     num_tokens: Optional[int] = None, top_k: int = 10,
                     num_experts: int = 512) -> str:
-    """The kernel(s) one draft_moe_gemv call runs."""
-    if _one_launch(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts):
+    """The kernel(s) one draft_moe_gemv call (swizzled scales) runs."""
+    form = _form(hidden_size, intermediate_size, fused, num_tokens, top_k, num_experts)
+    if form == "lean":
+        return "moe_lean_kernel"
+    if form == "fused":
         return "moe_fused_kernel"
     return "moe_up_kernel + moe_down_kernel + moe_sum_kernel"
 

@@ -358,11 +358,27 @@ int fnx_moe_workspace_bytes(int max_m, int max_routes, int num_experts, int H, i
                             fnx_moe_workspace_sizes* out);
 
 /* The form fnx_moe_gemv takes for (M, R, E, H, I) with a workspace that has counters:
- * *fused = 1 for the one-launch layer, with its weight-ring stages, consumer groups and
- * dynamic shared memory; *fused = 0 (and zeros) for the three-launch layer.  Exposed for
- * tests and launch accounting. */
+ * *fused = 2 for the decode-width one-launch layer and 1 for the general one, with its
+ * weight-ring stages, consumer groups and dynamic shared memory; *fused = 0 (and zeros)
+ * for the three-launch layer.  Exposed for tests and launch accounting. */
 int fnx_plan_moe(int M, int R, int E, int H, int I, int* fused, int* stages, int* groups,
                  int64_t* smem_bytes);
+
+/* Which one-launch MoE layer fnx_moe_gemv uses (process-wide), given a workspace with
+ * counters:
+ *  FNX_MOE_PATH_AUTO   the decode-width layer (moe_lean_kernel: every SM one CTA, each
+ *                      CTA's share of the layer's weight bytes in flight at once, the route
+ *                      sum done by the CTA that owns the output rows) for M = 1 with
+ *                      swizzled, 16-byte aligned block scales, H and I multiples of 256,
+ *                      I <= 512, H <= 2048; the general one-launch layer otherwise (the
+ *                      default);
+ *  FNX_MOE_PATH_FUSED  the general one-launch layer at every M.
+ * fnx_plan_moe reports *fused = 2 for the decode-width layer (assuming swizzled scales).
+ * *previous (may be NULL) receives the earlier setting.  No counterpart in the reference
+ * (its one-token MoE is two Triton launches). */
+#define FNX_MOE_PATH_AUTO 0
+#define FNX_MOE_PATH_FUSED 1
+int fnx_set_moe_path(int path, int* previous);
 
 /*
  * out[t, :] = sum_r topk_weights[t, r] * expert(topk_ids[t, r])(x[t]) [+ shared(x[t])]

@@ -109,8 +109,9 @@ def test_negative_ids_are_skipped_and_no_shared():
     assert rel_err(got[:2], ref[:2]) <= REL_TOL
 
 
+@pytest.mark.parametrize("path", ["auto", "fused"])
 @pytest.mark.parametrize("M", [1, 16])
-def test_deterministic_and_graph_replay(M):
+def test_deterministic_and_graph_replay(M, path):
     import flash_next_rtxpro6000_b200 as fx
     from flash_next_rtxpro6000_b200 import synthetic as syn
 
@@ -119,12 +120,23 @@ def test_deterministic_and_graph_replay(M):
     ids, wts = syn.routing(M, E=512, seed=70 + M)
     ids, wts = ids.to(dev()), wts.to(dev())
     ws = fx.make_workspace(num_routes=10, hidden_size=2048, intermediate_size=512, device=dev())
+    prev = fx.set_moe_path(path)
+    try:
+        _replay_checks(fx, syn, L, d, x, ids, wts, ws, M)
+    finally:
+        fx.set_moe_path(prev)
+
+
+def _replay_checks(fx, syn, L, d, x, ids, wts, ws, M):
     a = _run(fx, d, x, ids, wts, ws).clone()
     b = _run(fx, d, x, ids, wts, ws).clone()
     assert torch.equal(a, b)
-    # linear (unswizzled) scale layout gives the same bits
-    c = _run(fx, d, x, ids, wts, ws, linear=True)
-    assert torch.equal(a, c)
+    # linear (unswizzled) scale layout gives the same bits as the swizzled one in the
+    # general one-launch layer (the decode-width layer reads swizzled scales only)
+    with fx.moe_path("fused"):
+        a_f = _run(fx, d, x, ids, wts, ws).clone()
+        c = _run(fx, d, x, ids, wts, ws, linear=True)
+    assert torch.equal(a_f, c)
     xs, is_, ws_ = x.clone(), ids.clone(), wts.clone()
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -148,6 +160,7 @@ def test_deterministic_and_graph_replay(M):
     torch.cuda.synchronize()
     ref2 = _oracle(L, x2, ids2, wts2)
     assert rel_err(to_np(yg), ref2) <= REL_TOL
+    assert int(torch.count_nonzero(ws.counters)) == 0
     del g
 
 
