@@ -574,23 +574,23 @@ def _graph_of(calls, warm=3):
     return g
 
 
-def _roofline_per_m(per_m, peak, src, kernel, traffic_key=None):
+def _roofline_per_m(per_m, peak, src, kernel, traffic_key=None, traffic_per_m=None):
     """Roofline object of a workload measured at several M: achieved = total algorithmic
-    bytes / total launch time over the M values; per-M achieved / frac beside it;
-    traffic = ncu DRAM bytes per launch from profiles/ (averaged over the M values
-    captured), or None."""
+    bytes / total launch time over the M values; per-M achieved / frac (and ncu traffic
+    where captured) beside it; traffic = ncu DRAM bytes per launch from profiles/,
+    averaged over the M values, when every M value has a capture, else None."""
     tot_b = sum(v["bytes_per_call"] for v in per_m.values())
     tot_us = sum(v["us_per_call"] for v in per_m.values())
     ach = tot_b / (tot_us * 1e-6) / 1e9
-    tr = traffic_for(traffic_key) if traffic_key else None
-    traffic = None
-    if tr:
-        got = [tr[m] for m in per_m if m in tr]
-        traffic = round(sum(got) / len(got)) if got else None
+    tr = traffic_per_m if traffic_per_m is not None else (traffic_for(traffic_key) if traffic_key else None)
+    tr = tr or {}
+    got = [tr[m] for m in per_m if m in tr]
+    traffic = round(sum(got) / len(got)) if got and len(got) == len(per_m) else None
     return {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
             "frac": round(ach / peak, 4), "traffic": traffic, "peak_source": src,
             "kernel": kernel, "bytes_per_launch_avg": tot_b // len(per_m),
-            "per_m": {m: {"achieved": v["GBps"], "frac": round(v["GBps"] / peak, 4)}
+            "per_m": {m: dict({"achieved": v["GBps"], "frac": round(v["GBps"] / peak, 4)},
+                              **({"traffic": tr[m]} if m in tr else {}))
                       for m, v in per_m.items()}}
 
 
@@ -890,7 +890,7 @@ def _bench_moe_body(args, fx, syn, dev, cpu, L, d, shared, fused, ws):
            "roofline": _roofline_per_m(results, peak, src, " | ".join(dict.fromkeys(
                                            fx.moe_kernel_name(syn.HIDDEN, syn.INTER, fused,
                                                               num_tokens=M) for M in Ms)),
-                                       "moe_fused_config2" if fused else "moe_nvfp4_config2"),
+                                       traffic_per_m=_moe_traffic(fx, syn, fused, Ms)),
            "clocks": clocks, "gpu_launches": launches}
     if cpu:
         cb = {}
@@ -908,6 +908,19 @@ def _bench_moe_body(args, fx, syn, dev, cpu, L, d, shared, fused, ws):
                                          "restated: per route dequantise + gate/up + silu*up "
                                          "+ down, fp32, all host threads)"}
     return res
+
+
+def _moe_traffic(fx, syn, fused, Ms):
+    """ncu DRAM bytes per launch of the kernel each M runs, from its profiles/ summary."""
+    keys = {"moe_lean_kernel": "moe_lean_config2_m1", "moe_fused_kernel": "moe_fused_config2_m16",
+            "moe_up_kernel + moe_down_kernel + moe_sum_kernel": "moe_nvfp4_config2"}
+    out = {}
+    for M in Ms:
+        key = keys.get(fx.moe_kernel_name(syn.HIDDEN, syn.INTER, fused, num_tokens=M))
+        t = traffic_for(key) if key else None
+        if t and str(M) in t:
+            out[str(M)] = t[str(M)]
+    return out
 
 
 def _device_moe_layer(fx, syn, dev, seed, experts=None):
