@@ -217,3 +217,23 @@ def test_dense_path_selector():
             fx.set_dense_path("wgmma")
     finally:
         fx.set_dense_path(prev)
+
+
+def test_moe_form_selection():
+    """The one-token layer serves M = 1 with 256-multiple H and I (I <= 512, H <= 2048);
+    every other call, and every call under moe_path("fused"), takes the general
+    one-launch layer; an unknown path name is a ValueError (the ABI's FNX_EINVAL)."""
+    import flash_next_rtxpro6000_b200 as fx
+
+    assert fx.moe_plan(1, 10, 512, 2048, 512)["form"] == "lean"
+    assert fx.moe_kernel_name(2048, 512, True, num_tokens=1) == "moe_lean_kernel"
+    assert fx.moe_launches_per_call(2048, 512, num_tokens=1) == 1
+    for M, H, I in ((2, 2048, 512), (16, 2048, 512), (1, 2560, 640)):
+        assert fx.moe_plan(M, 10, 512, H, I)["form"] == "fused", (M, H, I)
+    p = fx.moe_plan(1, 10, 512, 2048, 512)
+    assert p["stages"] % p["groups"] == 0 and 0 < p["smem_bytes"] <= 227 * 1024
+    with fx.moe_path("fused"):
+        assert fx.moe_plan(1, 10, 512, 2048, 512)["form"] == "fused"
+    assert fx.moe_plan(1, 10, 512, 2048, 512)["form"] == "lean"
+    with pytest.raises(ValueError):
+        fx.set_moe_path("lean-ish")
