@@ -1,6 +1,6 @@
-// NVFP4 routed-MoE layer for one-token decode (M = 1; the code serves M <= 2) in ONE launch, laid out for
-// latency: the whole layer's weight bytes are cut into equal shares per SM and every CTA
-// puts its share in flight as soon as the routing is known.
+// NVFP4 routed-MoE layer for one-token decode (M = 1; the code serves M <= 2) in ONE
+// launch, laid out for latency: the whole layer's weight bytes are cut into equal shares
+// per SM and every CTA puts its share in flight as soon as the routing is known.
 //
 // Same operator and numerics as the reference's one-token pair (patches/sglang/series/
 // 0112-...patch:182-227 gate/up + SiLU, :229-287 down + route sum) and as moe_fused.cu:
