@@ -12,7 +12,7 @@ and CPU baseline, under ``workloads`` in the one JSON line (``--no-extra`` skips
     python bench.py [--gpus N] [--steps K] [--warmup W]
                     [--workload lm_head|draft_head|nvfp4|moe|norm_gated|router|draft_step|stack]
                     [--layers L]   # stack: L MoE layers + the lm_head per step (default 48)
-    python bench.py --impl reference ...   # the reference's CPU path (numpy restatement)
+    python bench.py --impl reference ...   # the reference's CPU path (torch restatement)
 
 With N > 1 (torchrun, one rank per GPU) the lm_head is vocab-sharded: each rank streams
 V/N rows and computes its shard's greedy keys, and the MAX of the keys over ranks is taken
