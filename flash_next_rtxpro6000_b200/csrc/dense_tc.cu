@@ -204,8 +204,12 @@ __device__ __forceinline__ int tc_cta_of(long long w, long long total, int G) {
 // Stage the M token rows as fp16 scaled by a power of two (exact), in the K-major
 // canonical layout of the B operand: 16-byte unit (k / 8, token) at ((k / 8) * 16 + token)
 // * 16.  Tokens M..15 are zero.  Warp gw of the `nwarps` staging warps takes tokens gw,
-// gw + nwarps, ...; ends with a proxy fence (the tensor core reads the rows through the
-// async proxy).
+// gw + nwarps, ...  A row of up to kTcHoldU units per lane (K <= 2048) is read once and
+// held in registers between its max and its conversion, so it costs one load round trip
+// (two for longer rows).  Ends with a proxy fence (the tensor core reads the rows through
+// the async proxy).
+constexpr int kTcHoldU = 8;
+
 __device__ __forceinline__ void tc_stage_x(uint8_t* xs, float* unscale, const DenseArgs& a,
                                            int gw, int nwarps, int lane) {
   const int K = a.K, nu = K / 8;
@@ -214,14 +218,35 @@ __device__ __forceinline__ void tc_stage_x(uint8_t* xs, float* unscale, const De
     if (m < a.M) {
       const uint8_t* row = reinterpret_cast<const uint8_t*>(x + (size_t)m * a.ldx);
       float mx = 0.f;
-      for (int u = lane; u < nu; u += 32) mx = fmaxf(mx, bf16x8_absmax(ldg_cg_u4(row + (size_t)u * 16)));
+      if (nu <= 32 * kTcHoldU) {
+        uint4 v[kTcHoldU];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const int e = stage_exponent(mx);
-      for (int u = lane; u < nu; u += 32)
-        *reinterpret_cast<uint4*>(xs + ((size_t)u * kTcN + m) * 16) =
-            bf16x8_to_f16x8_scaled(ldg_cg_u4(row + (size_t)u * 16), e);
-      if (lane == 0) unscale[m] = pow2f(-e);
+        for (int j = 0; j < kTcHoldU; ++j) {  // every load of the row in flight at once
+          const int u = lane + 32 * j;
+          v[j] = u < nu ? ldg_cg_u4(row + (size_t)u * 16) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < kTcHoldU; ++j) mx = fmaxf(mx, bf16x8_absmax(v[j]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int e = stage_exponent(mx);
+#pragma unroll
+        for (int j = 0; j < kTcHoldU; ++j) {
+          const int u = lane + 32 * j;
+          if (u < nu)
+            *reinterpret_cast<uint4*>(xs + ((size_t)u * kTcN + m) * 16) = bf16x8_to_f16x8_scaled(v[j], e);
+        }
+        if (lane == 0) unscale[m] = pow2f(-e);
+      } else {
+        for (int u = lane; u < nu; u += 32) mx = fmaxf(mx, bf16x8_absmax(ldg_cg_u4(row + (size_t)u * 16)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int e = stage_exponent(mx);
+        for (int u = lane; u < nu; u += 32)
+          *reinterpret_cast<uint4*>(xs + ((size_t)u * kTcN + m) * 16) =
+              bf16x8_to_f16x8_scaled(ldg_cg_u4(row + (size_t)u * 16), e);
+        if (lane == 0) unscale[m] = pow2f(-e);
+      }
     } else {
       for (int u = lane; u < nu; u += 32)
         *reinterpret_cast<uint4*>(xs + ((size_t)u * kTcN + m) * 16) = make_uint4(0u, 0u, 0u, 0u);
