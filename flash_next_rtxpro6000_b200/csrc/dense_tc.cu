@@ -283,7 +283,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) dense_tc_kernel(const __grid_co
   const long long lo = (long long)cta * total / G, hi = (long long)(cta + 1) * total / G;
   const int nchunk = (int)(hi - lo);
 
+  // One chunk of weights: one or two boxes of 128 rows x 128 bytes into ring stage s.
+  // The last chunk of a row holds one box when K is an odd multiple of 128.
+  auto issue_chunk = [&](int i, uint64_t pol) {
+    const int s = i % NS;
+    const long long w = lo + i;
+    const int b = (int)(w / KC), kc = (int)(w - (long long)b * KC);
+    const bool two = K - kc * kTcChunkK > kTcBoxK;
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(two ? kTcChunkBytes : kTcBoxBytes));
+    uint8_t* st = stages + (size_t)s * kTcChunkBytes;
+    tma_load_2d(st, &A.wmap, kc * kTcChunkK, b * kTcRows, &full[s], pol);
+    if (two) tma_load_2d(st + kTcBoxBytes, &A.wmap, kc * kTcChunkK + kTcBoxK, b * kTcRows, &full[s], pol);
+  };
+  // The producer lane fills the whole ring before the tensor-memory allocation and the
+  // block barrier: the weights do not depend on the previous kernel, and the first boxes
+  // are then in flight ~0.6 us earlier.
+  int pre = 0;
   if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&A.wmap)) : "memory");
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kTcConv);
@@ -299,6 +316,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) dense_tc_kernel(const __grid_co
     mbar_init(xready, kTcConv + kTcEpi);
     mbar_init(mmadone, 1);
     mbar_fence_init();
+    fence_proxy_async_smem();  // the initialised barriers are seen by the copy engine
+    const uint64_t pol = policy_evict_first();
+    pre = nchunk < NS ? nchunk : NS;
+    for (int i = 0; i < pre; ++i) issue_chunk(i, pol);
+  } else if (warp >= 2) {
+    // Converters and epilogue warps stage the token rows meanwhile, so that their loads
+    // go out ahead of most of the ring's boxes rather than queue behind them.
+    pdl_wait();
+    tc_stage_x(xs, unscale, a, warp - 2, kTcConv + kTcEpi, lane);
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -316,22 +342,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) dense_tc_kernel(const __grid_co
     // The weights do not depend on the previous kernel: no dependency wait here.
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&A.wmap)) : "memory");
-      int issued = 0;
-      for (int i = 0; i < nchunk; ++i) {
+      int issued = pre;
+      for (int i = pre; i < nchunk; ++i) {
         const int s = i % NS;
-        if (i >= NS && !mbar_wait(&empty[s], ((i / NS) & 1) ^ 1)) {
+        if (!mbar_wait(&empty[s], ((i / NS) & 1) ^ 1)) {
           record_error(a.err, ERR_WAIT_EMPTY);
           break;
         }
-        const long long w = lo + i;
-        const int b = (int)(w / KC), kc = (int)(w - (long long)b * KC);
-        // the last chunk of a row holds one box when K is an odd multiple of 128
-        const bool two = K - kc * kTcChunkK > kTcBoxK;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(two ? kTcChunkBytes : kTcBoxBytes));
-        uint8_t* st = stages + (size_t)s * kTcChunkBytes;
-        tma_load_2d(st, &A.wmap, kc * kTcChunkK, b * kTcRows, &full[s], pol);
-        if (two) tma_load_2d(st + kTcBoxBytes, &A.wmap, kc * kTcChunkK + kTcBoxK, b * kTcRows, &full[s], pol);
+        issue_chunk(i, pol);
         issued = i + 1;
       }
       // no box may still be landing when the CTA exits
@@ -396,9 +414,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) dense_tc_kernel(const __grid_co
     tc_commit_elect(mmadone);
     if (!warp_wait(mmadone, 0) && lane == 0) record_error(a.err, ERR_DRAIN);
   } else {
-    // converters and epilogue warps stage the token rows first
-    pdl_wait();
-    tc_stage_x(xs, unscale, a, warp - 2, kTcConv + kTcEpi, lane);
+    // the token rows were staged before the block barrier (which made the barriers usable)
     __syncwarp();
     if (lane == 0) mbar_arrive(xready);
 
@@ -467,6 +483,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) dense_tc_kernel(const __grid_co
         const long long blk0 = (long long)b * KC, blk1 = blk0 + KC;
         const long long seg0 = w, seg1 = hi < blk1 ? hi : blk1;
         const int db = sg & 1;
+        const int n = b * kTcRows + rq;
+        // the row's scale is read while the block's MMAs run, not after them
+        const float s = per_row && n < N ? load_row_scale(a.scale, a.scale_kind, n) : scalar_scale;
         if (!warp_wait(&dfull[db], (sg >> 1) & 1)) {
           record_error(a.err, ERR_WAIT_RED);
           break;
@@ -488,37 +507,55 @@ __global__ void __launch_bounds__(kTcThreads, 1) dense_tc_kernel(const __grid_co
         if (lane == 0) mbar_arrive(&dfree[db]);
         bool fin = seg0 == blk0 && seg1 == blk1;
         if (!fin) {
-          // a block shared with other CTAs: publish this range's sums (slot 0 = the range
-          // starts inside the block, 1 = it starts at the block's first chunk)
-          const int ht = seg0 > blk0 ? 0 : 1;
-          float* slot = A.part + (((size_t)cta * 2 + ht) * kTcRows + rq) * kTcN;
-#pragma unroll
-          for (int m = 0; m < kTcN; ++m) st_cg_f32(slot + m, v[m]);
-          __threadfence();
-          __syncwarp();
+          // A block shared with other CTAs.  Its ranges are counted in chunks on the
+          // counter of the CTA that holds its first chunk; each range's sums go to a slot
+          // (0 = the range starts inside the block, 1 = it starts at the block's first
+          // chunk), and the last range to arrive adds the slots in k order.  A range that
+          // finds every other range already counted is the last one without publishing
+          // its own sums (the usual case for a CTA's final block, whose other part the
+          // next CTA ran at its start).
           const int c0 = tc_cta_of(blk0, total, G);
           const unsigned nseg = (unsigned)(seg1 - seg0);
-          unsigned prev = 0;
-          if (lane == 0) prev = atomicAdd(&A.pcnt[c0 * 4 + q], nseg);
-          prev = __shfl_sync(0xffffffffu, prev, 0);
-          fin = prev + nseg == (unsigned)KC;
-          if (fin) {  // the last contributor: sum the slots in k order
+          unsigned seen = 0;
+          if (lane == 0) seen = ld_acquire_gpu_u32(&A.pcnt[c0 * 4 + q]);
+          seen = __shfl_sync(0xffffffffu, seen, 0);
+          fin = seen + nseg == (unsigned)KC;
+          if (!fin) {
+            const int ht = seg0 > blk0 ? 0 : 1;
+            float* slot = A.part + (((size_t)cta * 2 + ht) * kTcRows + rq) * kTcN;
+#pragma unroll
+            for (int m = 0; m < kTcN; ++m) st_cg_f32(slot + m, v[m]);
             __threadfence();
+            __syncwarp();
+            unsigned prev = 0;
+            if (lane == 0) prev = atomicAdd(&A.pcnt[c0 * 4 + q], nseg);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            fin = prev + nseg == (unsigned)KC;
+            if (fin) __threadfence();
+          }
+          __syncwarp();
+          if (fin) {  // sum the ranges in k order (this CTA's own from registers)
             const int c1 = tc_cta_of(blk1 - 1, total, G);
+            float t[kTcN];
 #pragma unroll
-            for (int m = 0; m < kTcN; ++m) v[m] = 0.f;
+            for (int m = 0; m < kTcN; ++m) t[m] = 0.f;
             for (int cc = c0; cc <= c1; ++cc) {
-              const float* sp = A.part + (((size_t)cc * 2 + (cc == c0 ? 1 : 0)) * kTcRows + rq) * kTcN;
+              if (cc == cta) {
 #pragma unroll
-              for (int m = 0; m < kTcN; ++m) v[m] += ld_cg_f32(sp + m);
+                for (int m = 0; m < kTcN; ++m) t[m] += v[m];
+              } else {
+                const float* sp = A.part + (((size_t)cc * 2 + (cc == c0 ? 1 : 0)) * kTcRows + rq) * kTcN;
+#pragma unroll
+                for (int m = 0; m < kTcN; ++m) t[m] += ld_cg_f32(sp + m);
+              }
             }
+#pragma unroll
+            for (int m = 0; m < kTcN; ++m) v[m] = t[m];
             __syncwarp();
             if (lane == 0) A.pcnt[c0 * 4 + q] = 0u;
           }
         }
-        const int n = b * kTcRows + rq;
         if (fin && n < N) {
-          const float s = per_row ? load_row_scale(a.scale, a.scale_kind, n) : scalar_scale;
           void* dst = a.y;
           int64_t ld = a.ldy, col = n;
           if (a.split_n > 0 && n >= a.split_n) {

@@ -649,6 +649,15 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Load with acquire semantics at GPU scope: writes released before the value this load
+// returns (by a release or acq_rel atomic, or a fence ahead of a relaxed one) are visible to
+// this thread's later reads.
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Atomic add with acquire-release semantics at GPU scope: this thread's earlier writes
 // (and those ordered before them, e.g. by __syncwarp) are visible to whoever observes the
 // new value, and the returned old value carries the writes of earlier releasers.
